@@ -1,0 +1,202 @@
+"""ctypes binding of the detkernels_b200 C ABI (include/detkernels_b200.h).
+
+Loads the in-tree ``libdetkernels_b200.so``.  There is no fallback: if the
+library is missing every op raises, on any machine.  Torch is used only for
+device memory, the current stream and tensor metadata.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+# ---- status / dtype codes (mirror include/detkernels_b200.h) ----
+DK_OK = 0
+DK_ERR_INVALID_ARGUMENT = 1
+DK_ERR_UNSUPPORTED = 2
+DK_ERR_WORKSPACE = 3
+DK_ERR_CUDA = 4
+DK_ERR_DEVICE_TIMEOUT = 5
+DK_ERR_DEVICE_CHECK = 6
+
+DK_F32 = 0
+DK_F16 = 1
+DK_BF16 = 2
+
+MATMUL_K_SLICES = 8
+ATTN_KV_SPLIT = 256
+
+_c_void_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_int = ctypes.c_int
+_f32 = ctypes.c_float
+_size = ctypes.c_size_t
+
+# name -> (restype, argtypes); every symbol declared in include/detkernels_b200.h
+SIGNATURES = {
+    "dk_abi_version": (_int, []),
+    "dk_last_error": (ctypes.c_char_p, []),
+    "dk_device_status": (_int, [_int, _int, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
+    "dk_num_sms": (_int, [_int, ctypes.POINTER(_int)]),
+    "dk_kernel_attributes": (_int, [_int, ctypes.POINTER(_int), ctypes.POINTER(_int), ctypes.POINTER(_int),
+                                    ctypes.POINTER(_int)]),
+    "dk_rmsnorm_batch_invariant": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _int,
+                                          _f32, _c_void_p]),
+    "dk_rmsnorm_variant_workspace_size": (_size, [_i64]),
+    "dk_rmsnorm_batch_variant": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _int, _f32,
+                                        _int, _int, _c_void_p, _size, _c_void_p]),
+    "dk_matmul_workspace_size": (_size, [_i64, _i64, _i64]),
+    "dk_matmul_batch_invariant": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _i64, _int,
+                                         _c_void_p, _size, _c_void_p]),
+    "dk_matmul_slice_partials": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _int, _int,
+                                        _int, _c_void_p]),
+    "dk_matmul_fold_slices": (_int, [_c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p]),
+    "dk_matmul_variant_workspace_size": (_size, [_i64, _i64]),
+    "dk_matmul_batch_variant": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _i64, _int,
+                                       _int, _int, _c_void_p, _size, _c_void_p]),
+    "dk_attention_workspace_size": (_size, [_i32, _i32, _i32, _i32, _i32, _i32]),
+    "dk_attention_batch_invariant": (_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64,
+                                            _i64, _c_void_p, _i64, _i64, _c_void_p, _i32, _c_void_p, _i32, _i32,
+                                            _i32, _i32, _i32, _i32, _f32, _int, _c_void_p, _size, _c_void_p]),
+    "dk_attention_variant_workspace_size": (_size, [_i32, _i32, _i32]),
+    "dk_attention_batch_variant": (_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p,
+                                          _i64, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _int, _c_void_p, _size,
+                                          _c_void_p]),
+}
+
+
+class DetKernelsError(RuntimeError):
+    """A non-zero status from the C ABI or from the device status word."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def library_path() -> str:
+    return _build.LIB_PATH
+
+
+def load():
+    """Load (building first if this checkout has nvcc and a stale library)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = library_path()
+        if not os.path.exists(path):
+            raise DetKernelsError(
+                DK_ERR_CUDA,
+                "detkernels_b200: %s is not built; run `python -m detkernels_b200.build` "
+                "(there is no CPU or eager fallback)" % path)
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    msg = load().dk_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str) -> None:
+    if rc == DK_OK:
+        return
+    msg = "%s failed (code %d): %s" % (what, rc, last_error())
+    if rc == DK_ERR_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    if rc == DK_ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise DetKernelsError(rc, msg)
+
+
+def device_status(device: int, clear: bool = True):
+    """(code, detail) of the device status word; synchronises the device."""
+    code = _int(0)
+    detail = _int(0)
+    check(load().dk_device_status(int(device), 1 if clear else 0, ctypes.byref(code), ctypes.byref(detail)),
+          "dk_device_status")
+    return code.value, detail.value
+
+
+def raise_on_device_error(device: int) -> None:
+    code, detail = device_status(device, clear=True)
+    if code != DK_OK:
+        if code in (DK_ERR_DEVICE_TIMEOUT, DK_ERR_DEVICE_CHECK):
+            # scratch counters may be mid-update; start from clean workspaces
+            reset_workspaces(device)
+        raise DetKernelsError(code, "device status %d (detail 0x%x) on cuda:%d" % (code, detail, device))
+
+
+# ---- torch glue ----
+def dtype_code(dtype) -> int:
+    import torch
+    if dtype == torch.float32:
+        return DK_F32
+    if dtype == torch.float16:
+        return DK_F16
+    if dtype == torch.bfloat16:
+        return DK_BF16
+    raise NotImplementedError("detkernels_b200: unsupported dtype %s" % (dtype,))
+
+
+def stream_ptr(device=None) -> int:
+    import torch
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+_workspaces = {}
+_ws_lock = threading.Lock()
+
+
+def workspace(nbytes: int, device, stream: int):
+    """Zero-initialised scratch buffer of >= nbytes for (device, stream).
+
+    Arrival counters inside the scratch reset themselves at the end of every
+    launch, so a buffer is reused as is.  Calls that overlap on different
+    streams get different buffers."""
+    import torch
+    if nbytes <= 0:
+        return None
+    dev = torch.device(device)
+    key = (dev.index, stream)
+    with _ws_lock:
+        buf = _workspaces.get(key)
+        if buf is None or buf.numel() < nbytes:
+            size = max(int(nbytes), 1 << 20)
+            if buf is not None:
+                size = max(size, 2 * buf.numel())
+            buf = torch.zeros(size, dtype=torch.uint8, device=dev)
+            _workspaces[key] = buf
+        return buf
+
+
+def reset_workspaces(device=None) -> None:
+    with _ws_lock:
+        for key in list(_workspaces):
+            if device is None or key[0] == device:
+                _workspaces[key].zero_()
+
+
+def exported_symbols():
+    return list(SIGNATURES)
+
+
+def kernel_attributes(which: int):
+    """(registers/thread, max threads/block, local bytes, max dynamic smem) of a compiled kernel."""
+    vals = [_int(0) for _ in range(4)]
+    check(load().dk_kernel_attributes(int(which), *[ctypes.byref(v) for v in vals]), "dk_kernel_attributes")
+    return tuple(v.value for v in vals)

@@ -1,0 +1,502 @@
+// Batch-invariant split-KV decode attention.
+//
+// Replaces kernels/attention.py:86-143 (_attn_direct_kernel) behind
+// attention_batch_invariant (attention.py:289-298), extended with grouped
+// query heads (GQA), per-row KV lengths and multi-row tiles (prefill rows of
+// one sequence processed together with exactly the per-row arithmetic of a
+// decode step).
+//
+// Fixed reduction structure (the definition of the output bits of a row):
+//   * The row's KV tokens [0, kv_len) are cut into splits of DK_ATTN_KV_SPLIT
+//     = 256 tokens (a fixed SIZE, so the split count follows the row's own
+//     length and nothing else).
+//   * Inside a split, tokens are visited in blocks of 64; warp w of the CTA
+//     always owns tokens [16w, 16w+16) of every block and keeps its own
+//     online-softmax state (running max m, running sum l, f32 accumulator O).
+//     Scores come from mma.m16n8k16 (bf16/f16 in, f32 accumulate) with the q
+//     vector as one of the 16 MMA rows; probabilities are rounded to the input
+//     type for the P.V product and the same rounded values are summed into l.
+//   * The four warp states are merged in warp order 0..3, the split states in
+//     split order, each with weights exp2(m_i - max_i m_i); out = O / l.
+// A row's arithmetic therefore depends on its q, its KV sequence and its
+// kv_len only -- not on the batch, the other rows of its tile, or the grid.
+//
+// Work decomposition: one CTA per (row tile, kv head, split).  A producer warp
+// streams 64-token K/V blocks with TMA (4-D tensor map over the cache, 128- or
+// 64-byte swizzle) into a ring of shared-memory stages; four consumer warps
+// compute.  Multi-split tiles write (m, l, O) partials to the workspace and the
+// last CTA to arrive (atomic counter, no spinning) combines them.
+#pragma once
+
+#include "dk_common.cuh"
+
+namespace dk {
+namespace attn {
+
+constexpr int kSplit = DK_ATTN_KV_SPLIT;
+constexpr int kBlock = 64;
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = 32 * (kConsumerWarps + 1);
+constexpr int kRows = 16;
+
+template <int D>
+struct Cfg {
+  static_assert(D == 32 || D == 64 || D == 128, "head_dim");
+  static constexpr int BOXD = D < 64 ? D : 64;          // elements per TMA box row
+  static constexpr int NBOX = D / BOXD;                 // boxes per tensor per block
+  static constexpr int ROWB = BOXD * 2;                 // bytes per token row in a box
+  static constexpr int CPB = ROWB / 16;                 // 16-byte chunks per box row
+  static constexpr int BOX_BYTES = kBlock * ROWB;
+  static constexpr int TENSOR_BYTES = NBOX * BOX_BYTES;  // 64 tokens x D
+  static constexpr int STAGE_BYTES = 2 * TENSOR_BYTES;   // K block + V block
+  static constexpr int STAGES = (D == 128) ? 3 : 4;
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int COMB_BYTES = kConsumerWarps * kRows * (D + 2) * 4;
+  static_assert(COMB_BYTES <= RING_BYTES, "combine scratch reuses the ring");
+  static constexpr int SMEM_BYTES = RING_BYTES + 1024 + 512;
+};
+
+struct Params {
+  const void* q;
+  int64_t q_sr, q_sh;
+  void* out;
+  int64_t o_sr, o_sh;
+  const int32_t* kv_lens;
+  int32_t uniform_len;
+  const int32_t* tiles;
+  int32_t n_tiles;
+  int32_t rows_cap;   // workspace rows per (tile, kv head, split) = rows_per_tile * G
+  int32_t n_rows, hq, hkv, G;
+  int32_t max_splits;
+  int32_t kv_capacity;
+  int32_t kv_n_seq;
+  float scale_log2;   // softmax scale * log2(e)
+  float* ws_o;        // [n_tiles][hkv][max_splits][rows_cap][D]
+  float* ws_ml;       // [n_tiles][hkv][max_splits][rows_cap][2]
+  int32_t* counters;  // [n_tiles][hkv]
+};
+
+enum : int {
+  kDetProdEmpty = 0x200,
+  kDetFull = 0x201,
+  kDetSync = 0x202,
+  kDetDrain = 0x203,
+  kDetLen = 0x210,   // a kv_len exceeds the cache capacity or max_kv_len
+  kDetTile = 0x211,  // a row tile is malformed
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Round two probabilities to the input type, pack them, and return the rounded values.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_round(float lo, float hi, float& rlo, float& rhi);
+template <>
+__device__ __forceinline__ uint32_t pack_round<__nv_bfloat16>(float lo, float hi, float& rlo, float& rhi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  rlo = __low2float(v);
+  rhi = __high2float(v);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack_round<__half>(float lo, float hi, float& rlo, float& rhi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  rlo = __low2float(v);
+  rhi = __high2float(v);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Shared-memory address of 16-byte chunk `c` (along d) of token row `r` inside
+// one tensor block of a stage, following the TMA swizzle of the box.
+template <int D>
+__device__ __forceinline__ uint32_t chunk_addr(uint32_t tensor_base, int r, int c) {
+  using C = Cfg<D>;
+  const int box = c / C::CPB;
+  const int cc = c % C::CPB;
+  const int swz = (C::ROWB == 128) ? (r & 7) : ((r >> 1) & 3);
+  return tensor_base + box * C::BOX_BYTES + r * C::ROWB + ((cc ^ swz) << 4);
+}
+
+// Bounded barrier among the 128 consumer threads.
+__device__ __forceinline__ bool csync(uint64_t* bar, uint32_t& phase, bool& abort_flag) {
+  if (abort_flag) return false;
+  mbar_arrive(bar);
+  const bool ok = mbar_wait(bar, phase, kDetSync, abort_flag);
+  phase ^= 1u;
+  return ok;
+}
+
+__device__ __forceinline__ float weight_of(float m, float mref) {
+  // exp2(m - mref); m == -inf gives 0.
+  return exp2f(__fsub_rn(m, mref));
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + C::RING_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* cbar = empty + C::STAGES;
+  int* s_len = reinterpret_cast<int*>(cbar + 1);   // kv_len of each tile row [16]
+  int* s_misc = s_len + kRows;                      // [0] last-arriver flag
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int tile = blockIdx.x / p.max_splits;
+  const int split = blockIdx.x % p.max_splits;
+  const int kvh = blockIdx.y;
+
+  // ---- tile description (identical in every CTA of the tile) ----
+  int r0, nr, seq;
+  if (p.tiles != nullptr) {
+    r0 = p.tiles[3 * tile + 0];
+    nr = p.tiles[3 * tile + 1];
+    seq = p.tiles[3 * tile + 2];
+  } else {
+    r0 = tile;
+    nr = 1;
+    seq = tile;
+  }
+  const int rows_per_tile_max = kRows / p.G;
+  if (nr < 1 || nr > rows_per_tile_max || r0 < 0 || r0 + nr > p.n_rows || seq < 0 || seq >= p.kv_n_seq ||
+      nr * p.G > p.rows_cap) {
+    if (threadIdx.x == 0 && split == 0 && kvh == 0) report_error(DK_ERR_DEVICE_CHECK, kDetTile);
+    return;
+  }
+  int max_len = 0;
+  bool len_bad = false;
+  for (int i = 0; i < nr; ++i) {
+    const int L = p.kv_lens ? p.kv_lens[r0 + i] : p.uniform_len;
+    if (L < 0 || L > p.kv_capacity || L > p.max_splits * kSplit) len_bad = true;
+    max_len = max(max_len, L);
+  }
+  if (len_bad) {
+    if (threadIdx.x == 0 && split == 0 && kvh == 0) report_error(DK_ERR_DEVICE_CHECK, kDetLen);
+    return;
+  }
+  const int nsplits = (max_len + kSplit - 1) / kSplit;
+  const int valid_rows = nr * p.G;
+  T* out = reinterpret_cast<T*>(p.out);
+
+  if (nsplits == 0) {
+    // every row of the tile has an empty KV sequence: output zeros
+    if (split == 0) {
+      for (int e = threadIdx.x; e < valid_rows * D; e += blockDim.x) {
+        const int rho = e / D, d = e % D;
+        const int i = rho / p.G, gh = rho % p.G;
+        out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(0.0f);
+      }
+    }
+    return;
+  }
+  if (split >= nsplits) return;
+
+  const int tok_begin = split * kSplit;
+  const int tok_end = min(tok_begin + kSplit, max_len);
+  const int nblk = (tok_end - tok_begin + kBlock - 1) / kBlock;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    mbar_init(cbar, kConsumerWarps * 32);
+    fence_mbar_init();
+  }
+  if (threadIdx.x < kRows) {
+    const int i = threadIdx.x;
+    s_len[i] = (i < nr) ? (p.kv_lens ? p.kv_lens[r0 + i] : p.uniform_len) : 0;
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      bool abort_flag = false;
+      int stage = 0;
+      uint32_t phase = 0;
+      int fills = 0;
+      for (int b = 0; b < nblk; ++b) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, kDetProdEmpty, abort_flag)) break;
+        uint8_t* st = ring + stage * C::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+        const int t0 = tok_begin + b * kBlock;
+#pragma unroll
+        for (int bx = 0; bx < C::NBOX; ++bx) {
+          tma_load_4d(st + bx * C::BOX_BYTES, &tmK, &full[stage], bx * C::BOXD, t0, kvh, seq);
+          tma_load_4d(st + C::TENSOR_BYTES + bx * C::BOX_BYTES, &tmV, &full[stage], bx * C::BOXD, t0, kvh, seq);
+        }
+        ++fills;
+        if (++stage == C::STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      bool drain_abort = false;
+      for (int f = (fills > C::STAGES ? fills - C::STAGES : 0); f < fills; ++f)
+        mbar_wait(&full[f % C::STAGES], static_cast<uint32_t>((f / C::STAGES) & 1), kDetDrain, drain_abort);
+    }
+    return;  // the producer warp takes no part in the combine
+  }
+
+  // ---------------- consumers ----------------
+  bool abort_flag = false;
+  const int g = lane >> 2;
+  const int t4 = lane & 3;
+  const int rho0 = g, rho1 = g + 8;
+  const bool v0 = rho0 < valid_rows, v1 = rho1 < valid_rows;
+  const int i0 = v0 ? rho0 / p.G : 0, i1 = v1 ? rho1 / p.G : 0;
+  const int end0 = v0 ? min(s_len[i0], tok_begin + kSplit) : 0;  // row's own token end in this split
+  const int end1 = v1 ? min(s_len[i1], tok_begin + kSplit) : 0;
+
+  // Q fragments (A operand, rows rho0/rho1), loaded once.
+  constexpr int KC = D / 16;
+  uint32_t qa[KC][4];
+  {
+    const T* q = reinterpret_cast<const T*>(p.q);
+    const T* q0 = v0 ? q + (int64_t)(r0 + i0) * p.q_sr + (int64_t)(kvh * p.G + rho0 % p.G) * p.q_sh : nullptr;
+    const T* q1 = v1 ? q + (int64_t)(r0 + i1) * p.q_sr + (int64_t)(kvh * p.G + rho1 % p.G) * p.q_sh : nullptr;
+#pragma unroll
+    for (int kc = 0; kc < KC; ++kc) {
+      const int d0 = kc * 16 + 2 * t4;
+      qa[kc][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d0) : 0u;
+      qa[kc][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d0) : 0u;
+      qa[kc][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d0 + 8) : 0u;
+      qa[kc][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d0 + 8) : 0u;
+    }
+  }
+
+  constexpr int NT = D / 8;  // output n-tiles of 8 along d
+  float o[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  float m_r[2] = {-INFINITY, -INFINITY};
+  float l_r[2] = {0.0f, 0.0f};
+
+  const int wr = warp * 16;  // this warp's first token row inside a block
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int b = 0; b < nblk; ++b) {
+    if (!mbar_wait(&full[stage], phase, kDetFull, abort_flag)) break;
+    const uint32_t kbase = smem_u32(ring + stage * C::STAGE_BYTES);
+    const uint32_t vbase = kbase + C::TENSOR_BYTES;
+    const int t0 = tok_begin + b * kBlock + wr;  // token of this warp's row 0
+
+    // Tokens no row of the tile may read: zero their V rows (K is masked by select).
+    const int tile_end = tok_end;
+    if (t0 + 16 > tile_end) {
+      uint8_t* vgen = ring + stage * C::STAGE_BYTES + C::TENSOR_BYTES;
+      for (int e = lane; e < 16 * (D / 8); e += 32) {
+        const int rr = e / (D / 8), c = e % (D / 8);
+        if (t0 + rr >= tile_end) {
+          const uint32_t a = chunk_addr<D>(0u, wr + rr, c);
+          *reinterpret_cast<uint4*>(vgen + a) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      // order these generic-proxy writes before the next TMA write of the stage
+      fence_proxy_async_smem();
+      __syncwarp();
+    }
+
+    // S = Q K^T for this warp's 16 tokens (two n-tiles of 8 tokens).
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kc = 0; kc < KC; ++kc) {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int r = wr + (mi >> 1) * 8 + ri;
+      const int c = 2 * kc + (mi & 1);
+      uint32_t b00, b01, b10, b11;
+      ldsm_x4(chunk_addr<D>(kbase, r, c), b00, b01, b10, b11);
+      mma16816<T>(s0, qa[kc], b00, b01);
+      mma16816<T>(s1, qa[kc], b10, b11);
+    }
+
+    // scale, mask, online softmax update (rows rho0 -> s*[0..1], rho1 -> s*[2..3])
+    const int tk = t0 + 2 * t4;
+    float sc[2][4];
+    sc[0][0] = (tk + 0 < end0) ? __fmul_rn(s0[0], p.scale_log2) : -INFINITY;
+    sc[0][1] = (tk + 1 < end0) ? __fmul_rn(s0[1], p.scale_log2) : -INFINITY;
+    sc[0][2] = (tk + 8 < end0) ? __fmul_rn(s1[0], p.scale_log2) : -INFINITY;
+    sc[0][3] = (tk + 9 < end0) ? __fmul_rn(s1[1], p.scale_log2) : -INFINITY;
+    sc[1][0] = (tk + 0 < end1) ? __fmul_rn(s0[2], p.scale_log2) : -INFINITY;
+    sc[1][1] = (tk + 1 < end1) ? __fmul_rn(s0[3], p.scale_log2) : -INFINITY;
+    sc[1][2] = (tk + 8 < end1) ? __fmul_rn(s1[2], p.scale_log2) : -INFINITY;
+    sc[1][3] = (tk + 9 < end1) ? __fmul_rn(s1[3], p.scale_log2) : -INFINITY;
+
+    uint32_t pa[4];
+    float alpha[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float mx = fmaxf(fmaxf(sc[h][0], sc[h][1]), fmaxf(sc[h][2], sc[h][3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_r[h], mx);
+      const float mref = (m_new == -INFINITY) ? 0.0f : m_new;
+      alpha[h] = weight_of(m_r[h], mref);
+      float pr[4];
+      const uint32_t lo = pack_round<T>(weight_of(sc[h][0], mref), weight_of(sc[h][1], mref), pr[0], pr[1]);
+      const uint32_t hi = pack_round<T>(weight_of(sc[h][2], mref), weight_of(sc[h][3], mref), pr[2], pr[3]);
+      pa[h] = lo;      // a0 (row g) / a1 (row g+8): tokens 2t, 2t+1
+      pa[h + 2] = hi;  // a2 / a3: tokens 8+2t, 8+2t+1
+      const float psum = __fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3]));
+      l_r[h] = __fadd_rn(__fmul_rn(l_r[h], alpha[h]), psum);
+      m_r[h] = m_new;
+    }
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      o[j][0] = __fmul_rn(o[j][0], alpha[0]);
+      o[j][1] = __fmul_rn(o[j][1], alpha[0]);
+      o[j][2] = __fmul_rn(o[j][2], alpha[1]);
+      o[j][3] = __fmul_rn(o[j][3], alpha[1]);
+    }
+    // O += P V
+#pragma unroll
+    for (int pc = 0; pc < D / 16; ++pc) {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int r = wr + (mi & 1) * 8 + ri;
+      const int c = 2 * pc + (mi >> 1);
+      uint32_t b0a, b1a, b0b, b1b;
+      ldsm_x4_t(chunk_addr<D>(vbase, r, c), b0a, b1a, b0b, b1b);
+      mma16816<T>(o[2 * pc], pa, b0a, b1a);
+      mma16816<T>(o[2 * pc + 1], pa, b0b, b1b);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == C::STAGES) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+
+  // quad-reduce l (fixed butterfly; m is already quad-uniform)
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 1));
+    l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 2));
+  }
+
+  // ---- merge the four warps in warp order ----
+  uint32_t cphase = 0;
+  const int ctid = threadIdx.x;  // 0..127
+  float* comb_o = reinterpret_cast<float*>(ring);                        // [4][16][D]
+  float* comb_ml = comb_o + kConsumerWarps * kRows * D;                  // [4][16][2]
+  csync(cbar, cphase, abort_flag);  // every warp is done reading the ring
+  if (!abort_flag) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int d = j * 8 + 2 * t4;
+      comb_o[(warp * kRows + rho0) * D + d] = o[j][0];
+      comb_o[(warp * kRows + rho0) * D + d + 1] = o[j][1];
+      comb_o[(warp * kRows + rho1) * D + d] = o[j][2];
+      comb_o[(warp * kRows + rho1) * D + d + 1] = o[j][3];
+    }
+    if (t4 == 0) {
+      comb_ml[(warp * kRows + rho0) * 2 + 0] = m_r[0];
+      comb_ml[(warp * kRows + rho0) * 2 + 1] = l_r[0];
+      comb_ml[(warp * kRows + rho1) * 2 + 0] = m_r[1];
+      comb_ml[(warp * kRows + rho1) * 2 + 1] = l_r[1];
+    }
+  }
+  csync(cbar, cphase, abort_flag);
+  if (abort_flag) return;
+
+  const int64_t slot = ((int64_t)tile * p.hkv + kvh) * p.max_splits;
+  for (int e = ctid; e < valid_rows * D; e += kConsumerWarps * 32) {
+    const int rho = e / D, d = e % D;
+    float mw[kConsumerWarps];
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      mw[w] = comb_ml[(w * kRows + rho) * 2];
+      M = fmaxf(M, mw[w]);
+    }
+    const float mref = (M == -INFINITY) ? 0.0f : M;
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float wt = weight_of(mw[w], mref);
+      L = __fadd_rn(L, __fmul_rn(comb_ml[(w * kRows + rho) * 2 + 1], wt));
+      O = __fadd_rn(O, __fmul_rn(comb_o[(w * kRows + rho) * D + d], wt));
+    }
+    const int i = rho / p.G, gh = rho % p.G;
+    if (nsplits == 1) {
+      const float r = (s_len[i] == 0) ? 0.0f : __fdiv_rn(O, L);
+      out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(r);
+    } else {
+      const int64_t base = (slot + split) * p.rows_cap + rho;
+      p.ws_o[base * D + d] = O;
+      if (d == 0) {
+        p.ws_ml[base * 2 + 0] = M;
+        p.ws_ml[base * 2 + 1] = L;
+      }
+    }
+  }
+  if (nsplits == 1) return;
+
+  // ---- cross-split combine by the last CTA of this (tile, kv head) ----
+  __threadfence();
+  if (!csync(cbar, cphase, abort_flag)) return;
+  if (ctid == 0) {
+    const int old = atomicAdd(p.counters + (int64_t)tile * p.hkv + kvh, 1);
+    const bool last = (old == nsplits - 1);
+    s_misc[0] = last ? 1 : 0;
+    if (last) p.counters[(int64_t)tile * p.hkv + kvh] = 0;
+  }
+  if (!csync(cbar, cphase, abort_flag)) return;
+  if (s_misc[0] == 0) return;
+  __threadfence();
+  for (int e = ctid; e < valid_rows * D; e += kConsumerWarps * 32) {
+    const int rho = e / D, d = e % D;
+    const int i = rho / p.G, gh = rho % p.G;
+    const int own = (s_len[i] + kSplit - 1) / kSplit;  // this row's own split count
+    float M = -INFINITY;
+    for (int s = 0; s < own; ++s) M = fmaxf(M, __ldcg(p.ws_ml + ((slot + s) * p.rows_cap + rho) * 2));
+    const float mref = (M == -INFINITY) ? 0.0f : M;
+    float L = 0.0f, O = 0.0f;
+    for (int s = 0; s < own; ++s) {
+      const int64_t base = (slot + s) * p.rows_cap + rho;
+      const float wt = weight_of(__ldcg(p.ws_ml + base * 2), mref);
+      L = __fadd_rn(L, __fmul_rn(__ldcg(p.ws_ml + base * 2 + 1), wt));
+      O = __fadd_rn(O, __fmul_rn(__ldcg(p.ws_o + base * D + d), wt));
+    }
+    const float r = (own == 0) ? 0.0f : __fdiv_rn(O, L);
+    out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(r);
+  }
+}
+
+}  // namespace attn
+}  // namespace dk

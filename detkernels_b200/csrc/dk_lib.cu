@@ -1,0 +1,707 @@
+// detkernels_b200 C ABI (see include/detkernels_b200.h).
+//
+// One translation unit: the kernels live in the dk_*.cuh headers; this file
+// holds argument validation, TMA tensor-map encoding, schedule selection and
+// the extern "C" entry points.  Nothing here allocates device memory: scratch
+// space comes from the caller's workspace.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "dk_common.cuh"
+#include "dk_rmsnorm.cuh"
+#include "dk_gemm.cuh"
+#include "dk_attention.cuh"
+#include "dk_attention_variant.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return DK_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int kMaxDevices = 64;
+
+// Every workspace starts with a fixed area of arrival counters shared by all
+// ops.  It must be zero when the workspace is first used; every call leaves it
+// zero again.  Non-counter scratch always lives after it, so calls with
+// different shapes never see each other's data in a counter.
+constexpr size_t kCounterBytes = DK_WORKSPACE_COUNTER_BYTES;
+constexpr int64_t kMaxCounters = static_cast<int64_t>(kCounterBytes / sizeof(int32_t));
+inline uint8_t* ws_data(void* ws) { return static_cast<uint8_t*>(ws) + kCounterBytes; }
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+int sm_count(int device) {
+  static int cache[kMaxDevices] = {0};
+  if (device < 0 || device >= kMaxDevices) return 148;
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) n = 148;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+// Raise the dynamic shared-memory limit of `fn` once per device.
+template <typename F>
+int ensure_smem(F fn, int bytes, bool (&done)[kMaxDevices]) {
+  const int dev = current_device();
+  if (dev >= 0 && dev < kMaxDevices && done[dev]) return DK_OK;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (dev >= 0 && dev < kMaxDevices) done[dev] = true;
+  return DK_OK;
+}
+
+// ---- TMA tensor maps through the driver entry point (no link-time libcuda dependency) ----
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+int encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(DK_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", what);
+  cuuint64_t gd[5], gs[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) gs[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, dt, rank, const_cast<void*>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DK_ERR_INVALID_ARGUMENT, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+  return DK_OK;
+}
+
+bool valid_dtype(int d) { return d == DK_F32 || d == DK_F16 || d == DK_BF16; }
+
+// ============================ RMSNorm ============================
+template <typename T, typename W>
+int rmsnorm_inv_launch(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int64_t cols,
+                       float eps, cudaStream_t st) {
+  constexpr int VEC = dk::Vec16<T>::N;
+  const bool vec = (cols % VEC == 0) && (xs % VEC == 0) && (ys % VEC == 0) && aligned16(x) && aligned16(y);
+  const dim3 grid(static_cast<unsigned>(rows));
+  if (vec) {
+    constexpr int MAXC = (sizeof(T) == 4) ? 8 : 4;
+    dk::rmsnorm_inv_vec_kernel<T, W, MAXC><<<grid, dk::kRmsThreads, 0, st>>>(
+        static_cast<const T*>(x), xs, static_cast<const W*>(w), static_cast<T*>(y), ys, cols, eps);
+  } else {
+    dk::rmsnorm_inv_scalar_kernel<T, W><<<grid, dk::kRmsThreads, 0, st>>>(
+        static_cast<const T*>(x), xs, static_cast<const W*>(w), static_cast<T*>(y), ys, cols, eps);
+  }
+  return check_launch("rmsnorm_batch_invariant");
+}
+
+template <typename T, typename W>
+int rmsnorm_var_launch(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int64_t cols,
+                       float eps, int n_splits, float* partial, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(partial, 0, sizeof(float) * rows, st);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "rmsnorm_batch_variant: memset: %s", cudaGetErrorString(e));
+  dk::rmsnorm_var_partial_kernel<T><<<dim3(static_cast<unsigned>(rows), n_splits), dk::kRmsThreads, 0, st>>>(
+      static_cast<const T*>(x), xs, partial, cols, n_splits);
+  dk::rmsnorm_var_finalize_kernel<T, W><<<dim3(static_cast<unsigned>(rows)), dk::kRmsThreads, 0, st>>>(
+      static_cast<const T*>(x), xs, static_cast<const W*>(w), partial, static_cast<T*>(y), ys, cols, eps);
+  return check_launch("rmsnorm_batch_variant");
+}
+
+int rms_validate(const void* x, const void* w, const void* y, int64_t xs, int64_t ys, int64_t rows, int64_t cols,
+                 int dtype, int wdtype, const char* what) {
+  if (!valid_dtype(dtype) || !valid_dtype(wdtype)) return fail(DK_ERR_UNSUPPORTED, "%s: bad dtype", what);
+  if (rows < 0 || cols <= 0) return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad shape [%lld, %lld]", what, (long long)rows,
+                                         (long long)cols);
+  if (rows > 0x7fffffffLL) return fail(DK_ERR_INVALID_ARGUMENT, "%s: too many rows", what);
+  if (rows > 0 && (!x || !w || !y)) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  if (rows > 1 && (xs < cols || ys < cols)) return fail(DK_ERR_INVALID_ARGUMENT, "%s: row stride < n_cols", what);
+  return DK_OK;
+}
+
+#define DK_DISPATCH_RMS(FN, ...)                                                                          \
+  do {                                                                                                    \
+    if (dtype == DK_F32) {                                                                                \
+      if (wdtype == DK_F32) return FN<float, float>(__VA_ARGS__);                                         \
+      if (wdtype == DK_F16) return FN<float, __half>(__VA_ARGS__);                                        \
+      return FN<float, __nv_bfloat16>(__VA_ARGS__);                                                       \
+    } else if (dtype == DK_F16) {                                                                         \
+      if (wdtype == DK_F32) return FN<__half, float>(__VA_ARGS__);                                        \
+      if (wdtype == DK_F16) return FN<__half, __half>(__VA_ARGS__);                                       \
+      return FN<__half, __nv_bfloat16>(__VA_ARGS__);                                                      \
+    } else {                                                                                              \
+      if (wdtype == DK_F32) return FN<__nv_bfloat16, float>(__VA_ARGS__);                                 \
+      if (wdtype == DK_F16) return FN<__nv_bfloat16, __half>(__VA_ARGS__);                                \
+      return FN<__nv_bfloat16, __nv_bfloat16>(__VA_ARGS__);                                               \
+    }                                                                                                     \
+  } while (0)
+
+// ============================ GEMM ============================
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+int slice_len_for(int64_t K, int n_slices) {
+  int64_t l = ceil_div(K, n_slices);
+  l = ceil_div(l, dk::gemm::kUK) * dk::gemm::kUK;
+  if (l < dk::gemm::kUK) l = dk::gemm::kUK;
+  return static_cast<int>(l);
+}
+
+struct GemmPlan {
+  int mode;
+  int group;
+  int n_tiles, m_tiles;
+  size_t ws_bytes;     // workspace bytes this plan needs
+  size_t counters_off; // byte offset of the counters region
+  size_t partials_off; // byte offset of the partials region
+};
+
+GemmPlan plan_invariant(int64_t M, int64_t N, int sms) {
+  GemmPlan pl{};
+  pl.n_tiles = static_cast<int>(ceil_div(N, dk::gemm::kTileN));
+  pl.m_tiles = static_cast<int>(ceil_div(M, dk::gemm::kTileM));
+  const int64_t tiles = static_cast<int64_t>(pl.n_tiles) * pl.m_tiles;
+  int group = dk::gemm::kSlices;
+  while (group > 1 && tiles * (dk::gemm::kSlices / group) < sms) group /= 2;
+  pl.group = group;
+  pl.mode = (group == dk::gemm::kSlices) ? dk::gemm::FOLD : dk::gemm::SPLIT;
+  if (pl.mode == dk::gemm::SPLIT) {
+    pl.counters_off = 0;
+    pl.partials_off = kCounterBytes;
+    pl.ws_bytes = pl.partials_off + sizeof(float) * static_cast<size_t>(dk::gemm::kSlices) * M * N;
+  }
+  return pl;
+}
+
+int gemm_validate(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N, int64_t K, int dtype,
+                  const char* what) {
+  if (dtype != DK_BF16 && dtype != DK_F16)
+    return fail(DK_ERR_UNSUPPORTED, "%s: dtype must be bf16 or f16", what);
+  if (M < 0 || N < 0 || K < 0 || M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad shape", what);
+  if (M == 0 || N == 0 || K == 0) return DK_OK;
+  if (!a || !b) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  if (!aligned16(a) || !aligned16(b)) return fail(DK_ERR_INVALID_ARGUMENT, "%s: A and B must be 16-byte aligned", what);
+  if (lda % 8 != 0 || ldb % 8 != 0)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: lda and ldb must be multiples of 8 elements", what);
+  if (lda < K || ldb < N) return fail(DK_ERR_INVALID_ARGUMENT, "%s: leading dimension too small", what);
+  return DK_OK;
+}
+
+int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb, dk::gemm::Params p,
+                cudaStream_t st, const char* what) {
+  CUtensorMap tmB, tmA;
+  const uint64_t dimsB[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K)};
+  const uint64_t strB[1] = {static_cast<uint64_t>(ldb) * 2};
+  const uint32_t boxB[2] = {64, static_cast<uint32_t>(dk::gemm::kBK)};
+  const uint64_t dimsA[2] = {static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M)};
+  const uint64_t strA[1] = {static_cast<uint64_t>(lda) * 2};
+  const uint32_t boxA[2] = {static_cast<uint32_t>(dk::gemm::kBK), static_cast<uint32_t>(dk::gemm::kTileM)};
+  const CUtensorMapDataType dt = (dtype == DK_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  int rc = encode_map(&tmB, dt, 2, b, dimsB, strB, boxB, CU_TENSOR_MAP_SWIZZLE_128B, what);
+  if (rc) return rc;
+  rc = encode_map(&tmA, dt, 2, a, dimsA, strA, boxA, CU_TENSOR_MAP_SWIZZLE_128B, what);
+  if (rc) return rc;
+
+  const int n_groups = (p.slice_end - p.slice_begin) / p.group;
+  const int64_t units = static_cast<int64_t>(p.n_tiles) * p.m_tiles * n_groups;
+  const int sms = sm_count(current_device());
+  const int grid = static_cast<int>(units < sms ? units : sms);
+  if (grid <= 0) return DK_OK;
+  if (dtype == DK_BF16) {
+    static bool done[kMaxDevices] = {false};
+    auto fn = dk::gemm::gemm_kernel<__nv_bfloat16, 1>;
+    if ((rc = ensure_smem(fn, dk::gemm::kSmemBytes, done))) return rc;
+    fn<<<grid, dk::gemm::kThreads, dk::gemm::kSmemBytes, st>>>(tmB, tmA, p);
+  } else {
+    static bool done[kMaxDevices] = {false};
+    auto fn = dk::gemm::gemm_kernel<__half, 0>;
+    if ((rc = ensure_smem(fn, dk::gemm::kSmemBytes, done))) return rc;
+    fn<<<grid, dk::gemm::kThreads, dk::gemm::kSmemBytes, st>>>(tmB, tmA, p);
+  }
+  return check_launch(what);
+}
+
+int zero_output(void* c, int64_t ldc, int64_t M, int64_t N, int elem, cudaStream_t st) {
+  if (M == 0 || N == 0) return DK_OK;
+  cudaError_t e = cudaMemset2DAsync(c, ldc * elem, 0, N * elem, M, st);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "matmul: memset: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
+
+template <typename T>
+int launch_fold(const float* partials, void* c, int64_t ldc, int M, int N, cudaStream_t st) {
+  const int64_t MN = static_cast<int64_t>(M) * N;
+  const int blocks = static_cast<int>(ceil_div(MN, 256) < 4096 ? ceil_div(MN, 256) : 4096);
+  dk::gemm::fold_slices_kernel<T><<<blocks, 256, 0, st>>>(partials, static_cast<T*>(c), ldc, M, N);
+  return check_launch("matmul_fold_slices");
+}
+
+template <typename T>
+int launch_cast(const float* src, void* c, int64_t ldc, int M, int N, cudaStream_t st) {
+  const int64_t MN = static_cast<int64_t>(M) * N;
+  const int blocks = static_cast<int>(ceil_div(MN, 256) < 4096 ? ceil_div(MN, 256) : 4096);
+  dk::gemm::cast_out_kernel<T><<<blocks, 256, 0, st>>>(src, static_cast<T*>(c), ldc, M, N);
+  return check_launch("matmul_batch_variant");
+}
+
+// ============================ attention ============================
+struct AttnPlan {
+  int n_tiles, rows_cap, max_splits;
+  size_t o_bytes, ml_bytes, cnt_bytes, total;
+};
+
+AttnPlan plan_attention(int32_t n_tiles, int32_t rows_per_tile, int32_t hq, int32_t hkv, int32_t D,
+                        int32_t max_kv_len) {
+  AttnPlan pl{};
+  const int G = (hkv > 0) ? hq / hkv : 1;
+  pl.n_tiles = n_tiles;
+  pl.rows_cap = (rows_per_tile <= 1) ? G : (dk::attn::kRows / G) * G;
+  pl.max_splits = static_cast<int>(ceil_div(max_kv_len > 0 ? max_kv_len : 1, dk::attn::kSplit));
+  const size_t slots = static_cast<size_t>(n_tiles) * hkv * pl.max_splits * pl.rows_cap;
+  pl.o_bytes = ceil_div(slots * D * sizeof(float), 256) * 256;
+  pl.ml_bytes = ceil_div(slots * 2 * sizeof(float), 256) * 256;
+  pl.cnt_bytes = static_cast<size_t>(n_tiles) * hkv * sizeof(int32_t);
+  // only multi-split work needs scratch; single-split rows write the output directly
+  pl.total = (pl.max_splits > 1) ? (kCounterBytes + pl.o_bytes + pl.ml_bytes) : 0;
+  return pl;
+}
+
+template <typename T, int D>
+int attn_launch(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int grid_x, int grid_y,
+                cudaStream_t st) {
+  using C = dk::attn::Cfg<D>;
+  static bool done[kMaxDevices] = {false};
+  auto fn = dk::attn::attn_kernel<T, D>;
+  int rc = ensure_smem(fn, C::SMEM_BYTES, done);
+  if (rc) return rc;
+  fn<<<dim3(grid_x, grid_y), dk::attn::kThreads, C::SMEM_BYTES, st>>>(tk, tv, p);
+  return check_launch("attention_batch_invariant");
+}
+
+}  // namespace
+
+// =====================================================================================
+extern "C" {
+
+int dk_abi_version(void) { return 1; }
+
+const char* dk_last_error(void) { return g_last_error.c_str(); }
+
+int dk_device_status(int device, int clear, int* code, int* detail) {
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return fail(DK_ERR_CUDA, "dk_device_status: no CUDA device");
+  if (cudaSetDevice(device) != cudaSuccess) return fail(DK_ERR_INVALID_ARGUMENT, "dk_device_status: bad device");
+  int c = 0, d = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&c, dk::g_status_code, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&d, dk::g_status_detail, sizeof(int));
+  if (e == cudaSuccess && clear) {
+    const int z = 0;
+    e = cudaMemcpyToSymbol(dk::g_status_code, &z, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(dk::g_status_detail, &z, sizeof(int));
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "dk_device_status: %s", cudaGetErrorString(e));
+  if (code) *code = c;
+  if (detail) *detail = d;
+  return DK_OK;
+}
+
+int dk_kernel_attributes(int which, int* num_regs, int* max_threads, int* local_bytes, int* max_dynamic_smem) {
+  cudaFuncAttributes a{};
+  cudaError_t e;
+  switch (which) {
+    case 0: e = cudaFuncGetAttributes(&a, dk::gemm::gemm_kernel<__nv_bfloat16, 1>); break;
+    case 1: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 128>); break;
+    case 2: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 64>); break;
+    case 3: e = cudaFuncGetAttributes(&a, dk::rmsnorm_inv_vec_kernel<float, float, 8>); break;
+    default: return fail(DK_ERR_INVALID_ARGUMENT, "dk_kernel_attributes: unknown kernel %d", which);
+  }
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "dk_kernel_attributes: %s", cudaGetErrorString(e));
+  if (num_regs) *num_regs = a.numRegs;
+  if (max_threads) *max_threads = a.maxThreadsPerBlock;
+  if (local_bytes) *local_bytes = static_cast<int>(a.localSizeBytes);
+  if (max_dynamic_smem) *max_dynamic_smem = a.maxDynamicSharedSizeBytes;
+  return DK_OK;
+}
+
+int dk_num_sms(int device, int* out) {
+  int n = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "dk_num_sms: %s", cudaGetErrorString(e));
+  if (out) *out = n;
+  return DK_OK;
+}
+
+// ---------------- RMSNorm ----------------
+int dk_rmsnorm_batch_invariant(const void* x, int64_t x_row_stride, const void* weight, void* out,
+                               int64_t out_row_stride, int64_t n_rows, int64_t n_cols, int dtype, int wdtype,
+                               float eps, void* stream) {
+  int rc = rms_validate(x, weight, out, x_row_stride, out_row_stride, n_rows, n_cols, dtype, wdtype,
+                        "rmsnorm_batch_invariant");
+  if (rc) return rc;
+  if (n_rows == 0) return DK_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  DK_DISPATCH_RMS(rmsnorm_inv_launch, x, x_row_stride, weight, out, out_row_stride, n_rows, n_cols, eps, st);
+}
+
+size_t dk_rmsnorm_variant_workspace_size(int64_t n_rows) {
+  return kCounterBytes + static_cast<size_t>(ceil_div((n_rows > 0 ? n_rows : 1) * 4, 256) * 256);
+}
+
+int dk_rmsnorm_batch_variant(const void* x, int64_t x_row_stride, const void* weight, void* out,
+                             int64_t out_row_stride, int64_t n_rows, int64_t n_cols, int dtype, int wdtype, float eps,
+                             int split_threshold, int n_splits, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  int rc = rms_validate(x, weight, out, x_row_stride, out_row_stride, n_rows, n_cols, dtype, wdtype,
+                        "rmsnorm_batch_variant");
+  if (rc) return rc;
+  if (n_rows == 0) return DK_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_rows >= split_threshold) {
+    DK_DISPATCH_RMS(rmsnorm_inv_launch, x, x_row_stride, weight, out, out_row_stride, n_rows, n_cols, eps, st);
+  }
+  if (n_splits < 1 || n_splits > 1024) return fail(DK_ERR_INVALID_ARGUMENT, "rmsnorm_batch_variant: bad n_splits");
+  if (!workspace || workspace_bytes < dk_rmsnorm_variant_workspace_size(n_rows))
+    return fail(DK_ERR_WORKSPACE, "rmsnorm_batch_variant: workspace too small");
+  float* partial = reinterpret_cast<float*>(ws_data(workspace));
+  DK_DISPATCH_RMS(rmsnorm_var_launch, x, x_row_stride, weight, out, out_row_stride, n_rows, n_cols, eps, n_splits,
+                  partial, st);
+}
+
+// ---------------- matmul ----------------
+size_t dk_matmul_workspace_size(int64_t M, int64_t N, int64_t K) {
+  (void)K;
+  if (M <= 0 || N <= 0) return 0;
+  return plan_invariant(M, N, sm_count(current_device())).ws_bytes;
+}
+
+size_t dk_matmul_variant_workspace_size(int64_t M, int64_t N) {
+  if (M <= 0 || N <= 0) return 0;
+  return kCounterBytes + static_cast<size_t>(ceil_div(M * N * 4, 256) * 256);
+}
+
+int dk_matmul_batch_invariant(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc, int64_t M,
+                              int64_t N, int64_t K, int dtype, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  const char* what = "matmul_batch_invariant";
+  int rc = gemm_validate(a, lda, b, ldb, M, N, K, dtype, what);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return DK_OK;
+  if (!c) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null output", what);
+  if (ldc < N) return fail(DK_ERR_INVALID_ARGUMENT, "%s: ldc < N", what);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) return zero_output(c, ldc, M, N, 2, st);
+  const GemmPlan pl = plan_invariant(M, N, sm_count(current_device()));
+  dk::gemm::Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.slice_len = slice_len_for(K, dk::gemm::kSlices);
+  p.slice_begin = 0;
+  p.slice_end = dk::gemm::kSlices;
+  p.group = pl.group;
+  p.n_tiles = pl.n_tiles;
+  p.m_tiles = pl.m_tiles;
+  p.mode = pl.mode;
+  p.c = c;
+  p.ldc = ldc;
+  if (pl.mode == dk::gemm::SPLIT) {
+    if (static_cast<int64_t>(pl.n_tiles) * pl.m_tiles > kMaxCounters)
+      return fail(DK_ERR_INVALID_ARGUMENT, "%s: too many output tiles for the counter area", what);
+    if (!workspace || workspace_bytes < pl.ws_bytes)
+      return fail(DK_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", what, pl.ws_bytes,
+                  workspace_bytes);
+    if (!aligned16(workspace)) return fail(DK_ERR_WORKSPACE, "%s: workspace must be 16-byte aligned", what);
+    p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + pl.counters_off);
+    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.partials_off);
+  }
+  return gemm_launch(dtype, a, lda, b, ldb, p, st, what);
+}
+
+int dk_matmul_slice_partials(const void* a, int64_t lda, const void* b, int64_t ldb, float* partials, int64_t M,
+                             int64_t N, int64_t K, int slice_begin, int slice_end, int dtype, void* stream) {
+  const char* what = "matmul_slice_partials";
+  int rc = gemm_validate(a, lda, b, ldb, M, N, K, dtype, what);
+  if (rc) return rc;
+  if (slice_begin < 0 || slice_end > dk::gemm::kSlices || slice_begin >= slice_end)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad slice range [%d, %d)", what, slice_begin, slice_end);
+  if (M == 0 || N == 0) return DK_OK;
+  if (!partials) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null partials", what);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    cudaError_t e = cudaMemsetAsync(partials, 0, sizeof(float) * (slice_end - slice_begin) * M * N, st);
+    return e == cudaSuccess ? DK_OK : fail(DK_ERR_CUDA, "%s: memset: %s", what, cudaGetErrorString(e));
+  }
+  dk::gemm::Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.slice_len = slice_len_for(K, dk::gemm::kSlices);
+  p.slice_begin = slice_begin;
+  p.slice_end = slice_end;
+  p.group = 1;
+  p.n_tiles = static_cast<int>(ceil_div(N, dk::gemm::kTileN));
+  p.m_tiles = static_cast<int>(ceil_div(M, dk::gemm::kTileM));
+  p.mode = dk::gemm::PARTIAL;
+  p.ws = partials;
+  return gemm_launch(dtype, a, lda, b, ldb, p, st, what);
+}
+
+int dk_matmul_fold_slices(const float* partials, void* c, int64_t ldc, int64_t M, int64_t N, int dtype,
+                          void* stream) {
+  if (dtype != DK_BF16 && dtype != DK_F16) return fail(DK_ERR_UNSUPPORTED, "matmul_fold_slices: bad dtype");
+  if (M < 0 || N < 0 || M > 0x7fffffffLL || N > 0x7fffffffLL)
+    return fail(DK_ERR_INVALID_ARGUMENT, "matmul_fold_slices: bad shape");
+  if (M == 0 || N == 0) return DK_OK;
+  if (!partials || !c || ldc < N) return fail(DK_ERR_INVALID_ARGUMENT, "matmul_fold_slices: bad pointer/ldc");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == DK_BF16) return launch_fold<__nv_bfloat16>(partials, c, ldc, (int)M, (int)N, st);
+  return launch_fold<__half>(partials, c, ldc, (int)M, (int)N, st);
+}
+
+int dk_matmul_batch_variant(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc, int64_t M,
+                            int64_t N, int64_t K, int dtype, int split_m_threshold, int split_k, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  const char* what = "matmul_batch_variant";
+  if (M >= split_m_threshold)
+    return dk_matmul_batch_invariant(a, lda, b, ldb, c, ldc, M, N, K, dtype, workspace, workspace_bytes, stream);
+  int rc = gemm_validate(a, lda, b, ldb, M, N, K, dtype, what);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return DK_OK;
+  if (!c || ldc < N) return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad output", what);
+  if (split_k < 1 || split_k > 64) return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad split_k", what);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) return zero_output(c, ldc, M, N, 2, st);
+  const size_t need = dk_matmul_variant_workspace_size(M, N);
+  if (!workspace || workspace_bytes < need)
+    return fail(DK_ERR_WORKSPACE, "%s: workspace of %zu bytes needed", what, need);
+  float* acc = reinterpret_cast<float*>(ws_data(workspace));
+  cudaError_t e = cudaMemsetAsync(acc, 0, sizeof(float) * M * N, st);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "%s: memset: %s", what, cudaGetErrorString(e));
+  dk::gemm::Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.slice_len = slice_len_for(K, split_k);
+  p.slice_begin = 0;
+  p.slice_end = split_k;
+  p.group = 1;
+  p.n_tiles = static_cast<int>(ceil_div(N, dk::gemm::kTileN));
+  p.m_tiles = static_cast<int>(ceil_div(M, dk::gemm::kTileM));
+  p.mode = dk::gemm::ATOMIC;
+  p.ws = acc;
+  rc = gemm_launch(dtype, a, lda, b, ldb, p, st, what);
+  if (rc) return rc;
+  if (dtype == DK_BF16) return launch_cast<__nv_bfloat16>(acc, c, ldc, (int)M, (int)N, st);
+  return launch_cast<__half>(acc, c, ldc, (int)M, (int)N, st);
+}
+
+// ---------------- attention ----------------
+size_t dk_attention_workspace_size(int32_t n_tiles, int32_t rows_per_tile, int32_t n_q_heads, int32_t n_kv_heads,
+                                   int32_t head_dim, int32_t max_kv_len) {
+  if (n_tiles <= 0 || n_kv_heads <= 0 || n_q_heads <= 0 || head_dim <= 0) return 0;
+  return plan_attention(n_tiles, rows_per_tile, n_q_heads, n_kv_heads, head_dim, max_kv_len).total;
+}
+
+int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_stride_head, const void* k,
+                                 const void* v, int64_t kv_stride_seq, int64_t kv_stride_head, int64_t kv_stride_tok,
+                                 int64_t kv_n_seq, int64_t kv_capacity, void* out, int64_t out_stride_row,
+                                 int64_t out_stride_head, const int32_t* kv_lens, int32_t uniform_kv_len,
+                                 const int32_t* row_tiles, int32_t n_tiles, int32_t n_rows, int32_t n_q_heads,
+                                 int32_t n_kv_heads, int32_t head_dim, int32_t max_kv_len, float scale, int dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  const char* what = "attention_batch_invariant";
+  if (dtype != DK_BF16 && dtype != DK_F16) return fail(DK_ERR_UNSUPPORTED, "%s: dtype must be bf16 or f16", what);
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128)
+    return fail(DK_ERR_UNSUPPORTED, "%s: head_dim %d not in {32, 64, 128}", what, head_dim);
+  if (n_rows < 0 || n_q_heads <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads != 0)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad head counts", what);
+  const int G = n_q_heads / n_kv_heads;
+  if (G > dk::attn::kRows) return fail(DK_ERR_UNSUPPORTED, "%s: more than 16 query heads per kv head", what);
+  if (n_kv_heads > 65535) return fail(DK_ERR_INVALID_ARGUMENT, "%s: too many kv heads", what);
+  if (n_rows == 0) return DK_OK;
+  if (!q || !k || !v || !out) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  if (max_kv_len < 0 || kv_capacity <= 0 || kv_n_seq <= 0 || kv_capacity > 0x7fffffffLL || kv_n_seq > 0x7fffffffLL)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad KV extents", what);
+  if (!kv_lens && (uniform_kv_len < 0 || uniform_kv_len > max_kv_len || uniform_kv_len > kv_capacity))
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: uniform_kv_len out of range", what);
+  if (!row_tiles) {
+    n_tiles = n_rows;
+    if (kv_n_seq < n_rows) return fail(DK_ERR_INVALID_ARGUMENT, "%s: fewer KV sequences than rows", what);
+  } else if (n_tiles <= 0) {
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: n_tiles must be positive with row_tiles", what);
+  }
+  if (!aligned16(k) || !aligned16(v)) return fail(DK_ERR_INVALID_ARGUMENT, "%s: K/V must be 16-byte aligned", what);
+  if ((kv_stride_tok * 2) % 16 || (kv_stride_head * 2) % 16 || (kv_stride_seq * 2) % 16)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: KV strides must be multiples of 8 elements", what);
+  if ((reinterpret_cast<uintptr_t>(q) & 3u) || (q_stride_row & 1) || (q_stride_head & 1))
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: q rows must be 4-byte aligned", what);
+
+  const AttnPlan pl = plan_attention(n_tiles, row_tiles ? 2 : 1, n_q_heads, n_kv_heads, head_dim, max_kv_len);
+  if (static_cast<int64_t>(pl.n_tiles) * pl.max_splits > 0x7fffffffLL)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: grid too large", what);
+  if (pl.total > 0 && (!workspace || workspace_bytes < pl.total))
+    return fail(DK_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", what, pl.total, workspace_bytes);
+  if (pl.total > 0 && !aligned16(workspace)) return fail(DK_ERR_WORKSPACE, "%s: workspace alignment", what);
+
+  dk::attn::Params p{};
+  p.q = q;
+  p.q_sr = q_stride_row;
+  p.q_sh = q_stride_head;
+  p.out = out;
+  p.o_sr = out_stride_row;
+  p.o_sh = out_stride_head;
+  p.kv_lens = kv_lens;
+  p.uniform_len = uniform_kv_len;
+  p.tiles = row_tiles;
+  p.n_tiles = n_tiles;
+  p.rows_cap = pl.rows_cap;
+  p.n_rows = n_rows;
+  p.hq = n_q_heads;
+  p.hkv = n_kv_heads;
+  p.G = G;
+  p.max_splits = pl.max_splits;
+  p.kv_capacity = static_cast<int32_t>(kv_capacity);
+  p.kv_n_seq = static_cast<int32_t>(kv_n_seq);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  if (pl.total > 0) {
+    if (static_cast<int64_t>(n_tiles) * n_kv_heads > kMaxCounters)
+      return fail(DK_ERR_INVALID_ARGUMENT, "%s: %d tiles x %d kv heads exceed the workspace counter area", what,
+                  n_tiles, n_kv_heads);
+    uint8_t* w = ws_data(workspace);
+    p.ws_o = reinterpret_cast<float*>(w);
+    p.ws_ml = reinterpret_cast<float*>(w + pl.o_bytes);
+    p.counters = static_cast<int32_t*>(workspace);
+  }
+
+  // K/V tensor maps: 4-D (d, token, kv head, sequence)
+  CUtensorMap tk, tv;
+  const int boxd = head_dim < 64 ? head_dim : 64;
+  const uint64_t dims[4] = {static_cast<uint64_t>(head_dim), static_cast<uint64_t>(kv_capacity),
+                            static_cast<uint64_t>(n_kv_heads), static_cast<uint64_t>(kv_n_seq)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(kv_stride_tok) * 2, static_cast<uint64_t>(kv_stride_head) * 2,
+                               static_cast<uint64_t>(kv_stride_seq) * 2};
+  const uint32_t box[4] = {static_cast<uint32_t>(boxd), static_cast<uint32_t>(dk::attn::kBlock), 1, 1};
+  const CUtensorMapSwizzle swz = (boxd == 64) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapDataType dt = (dtype == DK_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  int rc = encode_map(&tk, dt, 4, k, dims, strides, box, swz, what);
+  if (rc) return rc;
+  rc = encode_map(&tv, dt, 4, v, dims, strides, box, swz, what);
+  if (rc) return rc;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int gx = pl.n_tiles * pl.max_splits;
+  const int gy = n_kv_heads;
+  if (dtype == DK_BF16) {
+    if (head_dim == 32) return attn_launch<__nv_bfloat16, 32>(tk, tv, p, gx, gy, st);
+    if (head_dim == 64) return attn_launch<__nv_bfloat16, 64>(tk, tv, p, gx, gy, st);
+    return attn_launch<__nv_bfloat16, 128>(tk, tv, p, gx, gy, st);
+  }
+  if (head_dim == 32) return attn_launch<__half, 32>(tk, tv, p, gx, gy, st);
+  if (head_dim == 64) return attn_launch<__half, 64>(tk, tv, p, gx, gy, st);
+  return attn_launch<__half, 128>(tk, tv, p, gx, gy, st);
+}
+
+size_t dk_attention_variant_workspace_size(int32_t batch, int32_t n_heads, int32_t head_dim) {
+  if (batch <= 0 || n_heads <= 0 || head_dim <= 0) return 0;
+  const int64_t bh = static_cast<int64_t>(batch) * n_heads;
+  return kCounterBytes + static_cast<size_t>((2 * bh + bh * head_dim) * sizeof(float));
+}
+
+int dk_attention_batch_variant(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k, const void* v,
+                               int64_t kv_stride_b, int64_t kv_stride_h, int64_t kv_stride_s, void* out,
+                               int64_t out_stride_b, int64_t out_stride_h, int32_t batch, int32_t n_heads,
+                               int32_t seq_len, int32_t head_dim, float scale, int32_t split_s, int dtype,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  const char* what = "attention_batch_variant";
+  if (dtype != DK_BF16 && dtype != DK_F16 && dtype != DK_F32) return fail(DK_ERR_UNSUPPORTED, "%s: bad dtype", what);
+  if (batch < 0 || n_heads <= 0 || seq_len <= 0 || head_dim <= 0 || split_s < 1 || batch > 0x7fffffff ||
+      n_heads > 65535 || split_s > 65535)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad shape", what);
+  if (batch == 0) return DK_OK;
+  if (!q || !k || !v || !out) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  const size_t need = dk_attention_variant_workspace_size(batch, n_heads, head_dim);
+  if (!workspace || workspace_bytes < need) return fail(DK_ERR_WORKSPACE, "%s: workspace too small", what);
+  dk::attn_var::Params p{};
+  p.q = q;
+  p.q_sb = q_stride_b;
+  p.q_sh = q_stride_h;
+  p.k = k;
+  p.v = v;
+  p.kv_sb = kv_stride_b;
+  p.kv_sh = kv_stride_h;
+  p.kv_ss = kv_stride_s;
+  p.out = out;
+  p.o_sb = out_stride_b;
+  p.o_sh = out_stride_h;
+  p.B = batch;
+  p.H = n_heads;
+  p.S = seq_len;
+  p.D = head_dim;
+  p.n_splits = split_s;
+  p.scale = scale;
+  const int64_t bh = static_cast<int64_t>(batch) * n_heads;
+  p.m = reinterpret_cast<float*>(ws_data(workspace));
+  p.l = p.m + bh;
+  p.acc = p.l + bh;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int init_blocks = static_cast<int>(ceil_div(bh * head_dim, 256) < 4096 ? ceil_div(bh * head_dim, 256) : 4096);
+  dk::attn_var::var_init_kernel<<<init_blocks, 256, 0, st>>>(p.m, p.l, p.acc, bh, bh * head_dim);
+  const dim3 grid(batch, n_heads, split_s);
+  const size_t shm = sizeof(float) * (dk::attn_var::kThreads / 32) * head_dim;
+  if (shm > 48 * 1024) return fail(DK_ERR_UNSUPPORTED, "%s: head_dim too large", what);
+  const int fin_blocks = init_blocks;
+#define DK_VAR_LAUNCH(T)                                                                    \
+  dk::attn_var::var_max_kernel<T><<<grid, dk::attn_var::kThreads, 0, st>>>(p);              \
+  dk::attn_var::var_sumacc_kernel<T><<<grid, dk::attn_var::kThreads, shm, st>>>(p);         \
+  dk::attn_var::var_finalize_kernel<T><<<fin_blocks, 256, 0, st>>>(p);
+  if (dtype == DK_BF16) {
+    DK_VAR_LAUNCH(__nv_bfloat16)
+  } else if (dtype == DK_F16) {
+    DK_VAR_LAUNCH(__half)
+  } else {
+    DK_VAR_LAUNCH(float)
+  }
+#undef DK_VAR_LAUNCH
+  return check_launch(what);
+}
+
+}  // extern "C"

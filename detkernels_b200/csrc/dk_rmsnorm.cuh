@@ -1,0 +1,186 @@
+// RMSNorm kernels.
+//
+// Invariant kernel (replaces kernels/rmsnorm.py:63-89 _single_block_kernel):
+//   one CTA of 256 threads per row, always.  Thread t owns the 16-byte chunks
+//   t, t+256, t+512, ... of its row and accumulates x^2 over them in ascending
+//   order with fused multiply-adds; the 32 lanes of a warp are combined by an
+//   xor butterfly (16, 8, 4, 2, 1) and the 8 warp sums by a second butterfly
+//   (4, 2, 1).  Every step depends only on n_cols, so a row's bits never depend
+//   on n_rows.  var = sum / n_cols, rstd = 1 / sqrt(var + eps) (IEEE division
+//   and square root), y = (x * rstd) * w, rounded to the output dtype (RNE).
+//
+// Variant kernels (replace kernels/rmsnorm.py:91-138, dispatched as in
+//   rmsnorm.py:200-217): for small batches each row is split into n_splits
+//   chunks whose partial sums of squares are added with f32 atomics, so the
+//   summation order is decided by the scheduler.
+#pragma once
+
+#include "dk_common.cuh"
+
+namespace dk {
+
+constexpr int kRmsThreads = DK_RMSNORM_THREADS;
+
+template <typename T>
+struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+  T v[N];
+};
+
+__device__ __forceinline__ float block_sum_256(float acc, float* red) {
+  // fixed xor butterfly within the warp
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = acc;
+  __syncthreads();
+  float t = (lane < kRmsThreads / 32) ? red[lane] : 0.0f;
+  if (warp == 0) {
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+    if (lane == 0) red[8] = t;
+  }
+  __syncthreads();
+  return red[8];
+}
+
+// Vectorised path: every row pointer is 16-byte aligned and n_cols % VEC == 0.
+// MAXC chunks per thread are kept in registers; longer rows are re-read for the
+// normalisation pass (same arithmetic either way).
+template <typename T, typename W, int MAXC>
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_inv_vec_kernel(const T* __restrict__ x, int64_t xs,
+                                                                       const W* __restrict__ w,
+                                                                       T* __restrict__ y, int64_t ys,
+                                                                       int64_t n_cols, float eps) {
+  constexpr int VEC = Vec16<T>::N;
+  __shared__ float red[9];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * xs;
+  T* yr = y + row * ys;
+  const int64_t nchunks = n_cols / VEC;
+
+  Vec16<T> keep[MAXC];
+  float acc = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int64_t c = threadIdx.x + (int64_t)i * kRmsThreads;
+    if (c < nchunks) {
+      keep[i] = *reinterpret_cast<const Vec16<T>*>(xr + c * VEC);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float f = to_f32<T>(keep[i].v[j]);
+        acc = __fmaf_rn(f, f, acc);
+      }
+    }
+  }
+  for (int64_t c = threadIdx.x + (int64_t)MAXC * kRmsThreads; c < nchunks; c += kRmsThreads) {
+    Vec16<T> t = *reinterpret_cast<const Vec16<T>*>(xr + c * VEC);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float f = to_f32<T>(t.v[j]);
+      acc = __fmaf_rn(f, f, acc);
+    }
+  }
+  const float total = block_sum_256(acc, red);
+  const float var = __fdiv_rn(total, (float)n_cols);
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int64_t c = threadIdx.x + (int64_t)i * kRmsThreads;
+    if (c < nchunks) {
+      Vec16<T> o;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float xn = __fmul_rn(to_f32<T>(keep[i].v[j]), rstd);
+        o.v[j] = from_f32<T>(__fmul_rn(xn, to_f32<W>(w[c * VEC + j])));
+      }
+      *reinterpret_cast<Vec16<T>*>(yr + c * VEC) = o;
+    }
+  }
+  for (int64_t c = threadIdx.x + (int64_t)MAXC * kRmsThreads; c < nchunks; c += kRmsThreads) {
+    Vec16<T> t = *reinterpret_cast<const Vec16<T>*>(xr + c * VEC);
+    Vec16<T> o;
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float xn = __fmul_rn(to_f32<T>(t.v[j]), rstd);
+      o.v[j] = from_f32<T>(__fmul_rn(xn, to_f32<W>(w[c * VEC + j])));
+    }
+    *reinterpret_cast<Vec16<T>*>(yr + c * VEC) = o;
+  }
+}
+
+// Scalar path for unaligned rows or n_cols not a multiple of the vector width.
+// It walks the same 16-byte chunks in the same per-thread order as the vector
+// path (the last chunk may be short), so a row's bits do not depend on which
+// path its pointer alignment selected.
+template <typename T, typename W>
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_inv_scalar_kernel(const T* __restrict__ x, int64_t xs,
+                                                                          const W* __restrict__ w,
+                                                                          T* __restrict__ y, int64_t ys,
+                                                                          int64_t n_cols, float eps) {
+  constexpr int VEC = Vec16<T>::N;
+  __shared__ float red[9];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * xs;
+  T* yr = y + row * ys;
+  const int64_t nchunks = (n_cols + VEC - 1) / VEC;
+  float acc = 0.0f;
+  for (int64_t c = threadIdx.x; c < nchunks; c += kRmsThreads) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const int64_t e = c * VEC + j;
+      if (e < n_cols) {
+        const float f = to_f32<T>(xr[e]);
+        acc = __fmaf_rn(f, f, acc);
+      }
+    }
+  }
+  const float total = block_sum_256(acc, red);
+  const float var = __fdiv_rn(total, (float)n_cols);
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  for (int64_t e = threadIdx.x; e < n_cols; e += kRmsThreads) {
+    const float xn = __fmul_rn(to_f32<T>(xr[e]), rstd);
+    yr[e] = from_f32<T>(__fmul_rn(xn, to_f32<W>(w[e])));
+  }
+}
+
+// ---- batch-variant twin: split partial sums combined with atomics ----
+template <typename T>
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_var_partial_kernel(const T* __restrict__ x, int64_t xs,
+                                                                           float* __restrict__ partial,
+                                                                           int64_t n_cols, int n_splits) {
+  __shared__ float red[9];
+  const int64_t row = blockIdx.x;
+  const int split = blockIdx.y;
+  const int64_t chunk = (n_cols + n_splits - 1) / n_splits;
+  const int64_t lo = split * chunk;
+  const int64_t hi = (lo + chunk < n_cols) ? lo + chunk : n_cols;
+  const T* xr = x + row * xs;
+  float acc = 0.0f;
+  for (int64_t e = lo + threadIdx.x; e < hi; e += kRmsThreads) {
+    const float f = to_f32<T>(xr[e]);
+    acc = __fmaf_rn(f, f, acc);
+  }
+  const float total = block_sum_256(acc, red);
+  if (threadIdx.x == 0) atomicAdd(partial + row, total);
+}
+
+template <typename T, typename W>
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_var_finalize_kernel(const T* __restrict__ x, int64_t xs,
+                                                                            const W* __restrict__ w,
+                                                                            const float* __restrict__ partial,
+                                                                            T* __restrict__ y, int64_t ys,
+                                                                            int64_t n_cols, float eps) {
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * xs;
+  T* yr = y + row * ys;
+  const float var = __fdiv_rn(partial[row], (float)n_cols);
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  for (int64_t e = threadIdx.x; e < n_cols; e += kRmsThreads) {
+    const float xn = __fmul_rn(to_f32<T>(xr[e]), rstd);
+    yr[e] = from_f32<T>(__fmul_rn(xn, to_f32<W>(w[e])));
+  }
+}
+
+}  // namespace dk

@@ -1,0 +1,165 @@
+/*
+ * detkernels_b200 -- C ABI of the batch-invariant kernel library for NVIDIA B200 (sm_100a).
+ *
+ * Every entry point takes raw device pointers, element strides, sizes, a CUDA
+ * stream (passed as void*, i.e. a cudaStream_t) and, where the kernel needs
+ * scratch space, a caller-provided device workspace.  The library never
+ * allocates device memory.  Launches are asynchronous on the given stream; the
+ * return value reports argument validation and launch errors only.  Errors
+ * detected on the device (a bounded wait that expired, an index outside the
+ * caller's buffers) are recorded in a per-device status word that
+ * dk_device_status() reads and clears.
+ *
+ * Each compute entry point names the reference interface it replaces
+ * (AdityaShome/DetKernels, Python + Triton):
+ *   kernels/rmsnorm.py, kernels/matmul.py, kernels/attention.py.
+ *
+ * Batch invariance contract: for every entry point marked "invariant", the
+ * bits written for one output row depend only on that row's inputs (and, for
+ * attention, that row's own KV sequence and length) -- never on how many other
+ * rows are in the call, what they contain, or which work schedule the library
+ * picked for the call.
+ */
+#ifndef DETKERNELS_B200_H
+#define DETKERNELS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define DK_OK 0
+#define DK_ERR_INVALID_ARGUMENT 1 /* shape, stride, pointer or alignment rejected */
+#define DK_ERR_UNSUPPORTED 2      /* dtype / head_dim / size combination not built */
+#define DK_ERR_WORKSPACE 3        /* workspace missing or smaller than *_workspace_size() */
+#define DK_ERR_CUDA 4             /* a CUDA runtime or driver call failed */
+#define DK_ERR_DEVICE_TIMEOUT 5   /* a bounded device-side wait expired (see detail) */
+#define DK_ERR_DEVICE_CHECK 6     /* a device-side index check failed (see detail) */
+
+/* ---- workspaces ----
+ * Every workspace starts with DK_WORKSPACE_COUNTER_BYTES of arrival counters shared by all entry
+ * points.  Zero that area once when the workspace is created; every call leaves it zero again (after
+ * a device-side error, zero it again).  Scratch data always lives after it.  Calls that may overlap
+ * on the GPU (different streams) need different workspaces. */
+#define DK_WORKSPACE_COUNTER_BYTES (1u << 20)
+
+/* ---- dtype codes ---- */
+#define DK_F32 0
+#define DK_F16 1
+#define DK_BF16 2
+
+/* ---- fixed numerics of the invariant kernels (part of the output definition) ---- */
+#define DK_MATMUL_K_SLICES 8        /* K is reduced as 8 fixed slices, folded ((p0+p1)+p2)+... in f32 */
+#define DK_ATTN_KV_SPLIT 256        /* decode attention reduces KV in fixed splits of 256 tokens */
+#define DK_RMSNORM_THREADS 256      /* one CTA of 256 threads per row */
+
+/* ---- library / device queries ---- */
+int dk_abi_version(void);
+/* Message for the last non-zero return code on the calling host thread. */
+const char* dk_last_error(void);
+/* Reads the device status word of `device` (synchronises that device).  If
+ * `clear` is non-zero the word is reset to DK_OK afterwards. */
+int dk_device_status(int device, int clear, int* code, int* detail);
+int dk_num_sms(int device, int* out);
+/* Introspection of the compiled kernels on the current device (registers per thread, the
+ * launch-time thread limit, local-memory bytes, dynamic shared-memory limit).  which: 0 = bf16
+ * GEMM, 1 = bf16 attention d128, 2 = bf16 attention d64, 3 = f32 RMSNorm. */
+int dk_kernel_attributes(int which, int* num_regs, int* max_threads, int* local_bytes, int* max_dynamic_smem);
+
+/* ---- RMSNorm: y = x * rsqrt(mean(x^2) + eps) * w, f32 math, y in x's dtype ----
+ * x, out: [n_rows, n_cols] with unit column stride and the given row strides
+ * (elements).  dtype: DK_F32 / DK_F16 / DK_BF16 for x and out; weight_dtype
+ * for w (any of the three). */
+
+/* replaces kernels/rmsnorm.py:155-177 rmsnorm_batch_invariant (+ _single_block_kernel 63-89) */
+int dk_rmsnorm_batch_invariant(const void* x, int64_t x_row_stride, const void* weight, void* out,
+                               int64_t out_row_stride, int64_t n_rows, int64_t n_cols, int dtype,
+                               int weight_dtype, float eps, void* stream);
+
+/* Scratch bytes dk_rmsnorm_batch_variant needs for n_rows rows. */
+size_t dk_rmsnorm_variant_workspace_size(int64_t n_rows);
+/* replaces kernels/rmsnorm.py:180-218 rmsnorm_batch_variant: when n_rows < split_threshold each row's
+ * sum of squares is split into n_splits chunks combined with f32 atomics (order decided by the
+ * scheduler: deliberately NOT batch invariant); otherwise identical to the invariant kernel. */
+int dk_rmsnorm_batch_variant(const void* x, int64_t x_row_stride, const void* weight, void* out,
+                             int64_t out_row_stride, int64_t n_rows, int64_t n_cols, int dtype,
+                             int weight_dtype, float eps, int split_threshold, int n_splits,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Matmul: C[M,N] = A[M,K] @ B[K,N] (row-major, unit inner stride), f32 accumulate ----
+ * dtype: DK_BF16 or DK_F16 (A, B and C share it).  Row strides (lda, ldb, ldc)
+ * in elements; lda and ldb must be multiples of 8 and A, B 16-byte aligned
+ * (TMA).  The invariant kernel reduces K as DK_MATMUL_K_SLICES fixed slices of
+ * ceil16(K/8) elements, each accumulated by tcgen05 in ascending 16-wide K
+ * steps into its own f32 TMEM accumulator, then folded in slice order. */
+
+/* Scratch bytes the invariant / variant matmul may need for this shape. */
+size_t dk_matmul_workspace_size(int64_t M, int64_t N, int64_t K);
+/* replaces kernels/matmul.py:161-186 matmul_batch_invariant (+ _matmul_kernel 64-100) */
+int dk_matmul_batch_invariant(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+                              int64_t M, int64_t N, int64_t K, int dtype, void* workspace,
+                              size_t workspace_bytes, void* stream);
+/* Same numerics, but only slices [slice_begin, slice_end) are computed and each slice's f32
+ * partial is written to partials[(s - slice_begin) * M * N + m * N + n] (row-parallel tensor
+ * parallelism: every rank computes its own slices; dk_matmul_fold_slices sums them in order). */
+int dk_matmul_slice_partials(const void* a, int64_t lda, const void* b, int64_t ldb, float* partials,
+                             int64_t M, int64_t N, int64_t K, int slice_begin, int slice_end, int dtype,
+                             void* stream);
+/* out[m,n] = round(((p0 + p1) + p2) + ... + p7) with p_s = partials[s*M*N + m*N + n]. */
+int dk_matmul_fold_slices(const float* partials, void* c, int64_t ldc, int64_t M, int64_t N, int dtype,
+                          void* stream);
+/* Scratch bytes dk_matmul_batch_variant needs on its split-K path. */
+size_t dk_matmul_variant_workspace_size(int64_t M, int64_t N);
+/* replaces kernels/matmul.py:189-228 matmul_batch_variant: when M < split_m_threshold, K is split
+ * into split_k chunks whose f32 partials are combined with atomics (deliberately NOT batch
+ * invariant); otherwise the invariant kernel runs. */
+int dk_matmul_batch_variant(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+                            int64_t M, int64_t N, int64_t K, int dtype, int split_m_threshold, int split_k,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Decode attention (one query per row, split-KV with a fixed split size) ----
+ * q:   [n_rows, n_q_heads, head_dim], strides (q_stride_row, q_stride_head), unit d stride.
+ * k,v: KV cache viewed as [kv_n_seq, n_kv_heads, kv_capacity, head_dim] with element strides
+ *      (kv_stride_seq, kv_stride_head, kv_stride_tok), unit d stride; k and v share strides.
+ * out: [n_rows, n_q_heads, head_dim], strides (out_stride_row, out_stride_head).
+ * Row r attends to tokens [0, kv_len_r) of KV sequence seq_r, q head h uses kv head
+ * h / (n_q_heads / n_kv_heads).  kv_lens (device int32[n_rows]) may be NULL, then every row
+ * uses uniform_kv_len.  row_tiles (device int32[3 * n_tiles]: first row, row count, seq) groups
+ * consecutive rows that read the same KV sequence (at most 16 / group rows per tile); when NULL,
+ * row r is its own tile reading sequence r.  max_kv_len bounds every kv_len_r (sizes the grid).
+ * head_dim in {32, 64, 128}; dtype DK_BF16 or DK_F16; scale multiplies q.k. */
+/* Scratch bytes for a call with n_tiles tiles (n_rows when row_tiles is NULL) of up to rows_per_tile rows
+ * (1 without row_tiles); 0 when no row needs more than one split. */
+size_t dk_attention_workspace_size(int32_t n_tiles, int32_t rows_per_tile, int32_t n_q_heads, int32_t n_kv_heads,
+                                   int32_t head_dim, int32_t max_kv_len);
+/* replaces kernels/attention.py:289-298 attention_batch_invariant (+ _attn_direct_kernel 86-143,
+ * _run_direct 266-286), extended with GQA, per-row KV lengths and row tiles */
+int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_stride_head, const void* k,
+                                 const void* v, int64_t kv_stride_seq, int64_t kv_stride_head,
+                                 int64_t kv_stride_tok, int64_t kv_n_seq, int64_t kv_capacity, void* out,
+                                 int64_t out_stride_row, int64_t out_stride_head, const int32_t* kv_lens,
+                                 int32_t uniform_kv_len, const int32_t* row_tiles, int32_t n_tiles,
+                                 int32_t n_rows, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
+                                 int32_t max_kv_len, float scale, int dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* Scratch bytes dk_attention_batch_variant needs. */
+size_t dk_attention_variant_workspace_size(int32_t batch, int32_t n_heads, int32_t head_dim);
+/* replaces kernels/attention.py:145-249 (_attn_split_max_kernel, _attn_split_sumacc_kernel) as dispatched by
+ * attention_batch_variant (attention.py:301-348): q [batch, n_heads, head_dim], k/v [batch, n_heads, seq_len,
+ * head_dim] (unit d stride), KV cut into split_s chunks combined with f32 atomics -- deliberately NOT
+ * batch invariant.  dtype DK_F32 / DK_F16 / DK_BF16. */
+int dk_attention_batch_variant(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k, const void* v,
+                               int64_t kv_stride_b, int64_t kv_stride_h, int64_t kv_stride_s, void* out,
+                               int64_t out_stride_b, int64_t out_stride_h, int32_t batch, int32_t n_heads,
+                               int32_t seq_len, int32_t head_dim, float scale, int32_t split_s, int dtype,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DETKERNELS_B200_H */
