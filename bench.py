@@ -1,0 +1,439 @@
+#!/usr/bin/env python
+"""Benchmark of the batch-invariant decode path on B200: prints ONE JSON line.
+
+Workload (one "step"): greedy decoding of 128 tokens for 256 prompts per GPU
+with a random-init TinyModel (4 layers, d_model 1024, 16 heads x 64, SwiGLU
+2816, vocab 32000, bf16): one tracked 32-token prompt (rank 0) among prompts of
+U[16, 512] random tokens, prefilled as rows and decoded through the invariant
+RMSNorm / tcgen05 GEMM / split-KV attention kernels with the decode steps in
+one CUDA graph.  Multi-GPU runs shard independent requests (weak scaling, no
+collective in the data path); the device-timed max over ranks is reported.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the CPU path of the reference's algorithm (the
+numpy oracle) on the host cores for the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+MODEL = dict(vocab_size=32000, num_layers=4, num_heads=16, head_dim=64, mlp_hidden=2816, mlp="swiglu",
+             dtype="bfloat16", seed=0)
+BATCH_PER_GPU = 256
+TRACKED_LEN = 32
+OTHER_LEN = (16, 512)
+NEW_TOKENS = 128
+WORKLOAD_NAME = ("tinymodel-decode: 4L d1024 16x64 SwiGLU2816 vocab32000 bf16, 256 prompts/GPU "
+                 "(tracked 32 tok + 255 of U[16,512] tok), 128 greedy tokens")
+GEMM_SHAPES = [(m, n) for n in (4096, 11008) for m in (1, 8, 64, 256, 2048)]
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ----------------------------------------------------------------------------- inputs
+def make_prompts(rank: int, batch: int):
+    import numpy as np
+
+    vocab = MODEL["vocab_size"]
+    tracked = np.random.default_rng(0).integers(0, vocab, TRACKED_LEN).tolist()
+    rng = np.random.default_rng(10_000 + rank)
+    n_other = batch - 1 if rank == 0 else batch
+    others = [rng.integers(0, vocab, int(rng.integers(OTHER_LEN[0], OTHER_LEN[1] + 1))).tolist()
+              for _ in range(n_other)]
+    return ([tracked] + others) if rank == 0 else others
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", ",".join(str(g) for g in self.gpus)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for nm, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(nm)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- distributed
+def dist_setup(n_gpus):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- CPU baseline (oracle)
+def cpu_sample(prompts, n_tokens, model=None):
+    """Time the oracle's decode (numpy, all host threads) on a bounded sample,
+    with the weights of `model` (a CPU TinyModel of the workload by default)."""
+    from threadpoolctl import threadpool_limits
+
+    from detkernels_b200.kernels.tiny_model import TinyModel, TinyModelConfig
+    from oracle import ops as oracle
+
+    cores = len(os.sched_getaffinity(0))
+    if model is None:
+        model = TinyModel(TinyModelConfig(**MODEL), device="cpu")
+
+    def f(t):
+        return t.float().cpu().numpy()
+
+    w = {"embed": f(model.embed), "layers": [{k: f(v) for k, v in L.items()} for L in model.layers],
+         "norm_f_w": f(model.norm_f_w), "w_lm_head": f(model.w_lm_head)}
+    orc = oracle.TinyModelOracle(w, MODEL["num_heads"], MODEL["num_heads"], MODEL["head_dim"], mlp="swiglu",
+                                 dtype="bfloat16")
+    with threadpool_limits(limits=cores):
+        t0 = time.perf_counter()
+        toks, _ = orc.generate(prompts, n_tokens)
+        dt = time.perf_counter() - t0
+    n = len(prompts) * n_tokens
+    return {"value": n / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": "numpy oracle decode of %d prompts (lengths %s), %d greedy tokens each, %.1f s"
+                      % (len(prompts), [len(p) for p in prompts], n_tokens, dt)}, toks
+
+
+def cpu_sample_prompts():
+    """Bounded CPU sample: the tracked prompt and 7 co-batched prompts cut to 48 tokens."""
+    p = make_prompts(0, 8)
+    return [p[0]] + [q[:48] for q in p[1:]]
+
+
+# ----------------------------------------------------------------------------- GEMM vs cuBLAS
+def gemm_vs_cublas(iters=10):
+    import torch
+
+    from detkernels_b200.kernels.matmul import matmul_batch_invariant
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(0)
+    w_cache = {}
+    for (m, n) in GEMM_SHAPES:
+        if n not in w_cache:
+            w_cache[n] = (0.02 * torch.randn(4096, n, device=dev, generator=g)).to(torch.bfloat16)
+        w = w_cache[n]
+        a = torch.randn(m, 4096, device=dev, generator=g).to(torch.bfloat16)
+
+        def timed(fn):
+            for _ in range(3):
+                fn()
+            ts = []
+            for _ in range(iters):
+                flush.zero_()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                fn()
+                e.record()
+                e.synchronize()
+                ts.append(s.elapsed_time(e))
+            return statistics.median(ts)
+
+        t_ours = timed(lambda: matmul_batch_invariant(a, w))
+        t_cub = timed(lambda: torch.matmul(a, w))
+        flops = 2.0 * m * n * 4096
+        res["M=%d,N=%d" % (m, n)] = {"ours_tflops": round(flops / t_ours / 1e9, 2),
+                                     "cublas_tflops": round(flops / t_cub / 1e9, 2),
+                                     "ratio": round(t_cub / t_ours, 3),
+                                     "ours_us": round(t_ours * 1e3, 2), "cublas_us": round(t_cub * 1e3, 2)}
+    del flush
+    return res
+
+
+# ----------------------------------------------------------------------------- main arms
+def run_reference(args, rank, world):
+    """CPU path of the reference algorithm (numpy oracle), rank 0 only."""
+    if rank != 0:
+        return 0
+    prompts = cpu_sample_prompts()
+    vals = []
+    base = None
+    for i in range(args.warmup + args.steps):
+        cb, _ = cpu_sample(prompts, 16)
+        if i >= args.warmup:
+            vals.append(cb["value"])
+            base = cb
+    value = statistics.mean(vals)
+    base["value"] = value
+    line = {"impl": "reference", "metric": "BI decode tok/s", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD_NAME, "sample": base["sample"]},
+            "cpu_baseline": base,
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, rank, world, local):
+    import numpy as np
+    import torch
+
+    from detkernels_b200 import _lib
+    from detkernels_b200.kernels.tiny_model import TinyModel, TinyModelConfig
+
+    dev = torch.device("cuda", local)
+    model = TinyModel(TinyModelConfig(**MODEL), device=str(dev))
+    prompts = make_prompts(rank, BATCH_PER_GPU)
+    cap = max(len(p) for p in prompts) + NEW_TOKENS
+    eng = model.engine(BATCH_PER_GPU, max(cap, OTHER_LEN[1] + NEW_TOKENS))
+    plan = eng.plan(prompts)
+
+    # solo reference for the tracked prompt (divergence check)
+    solo = None
+    if rank == 0:
+        solo = model.generate([prompts[0]], NEW_TOKENS, "batch_invariant")[0].clone()
+
+    for _ in range(args.warmup):
+        eng.run(plan, NEW_TOKENS, timing=True)
+    torch.cuda.synchronize(dev)
+
+    sampler = ClockSampler(list(range(world)) if world > 1 else [torch.cuda.current_device()])
+    if rank == 0:
+        sampler.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    n0 = _lib.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    acc = {"ms": 0.0, "n": 0, "pending": False}
+
+    def collect():
+        # attention launch durations of the previous step, from events recorded inside
+        # its decode graph; read while this step's prefill already occupies the GPU
+        if acc["pending"]:
+            times = eng.attention_times_ms()
+            acc["ms"] += sum(times)
+            acc["n"] += len(times)
+            acc["pending"] = False
+
+    outs = []
+    start.record()
+    for _ in range(args.steps):
+        outs.append(eng.run(plan, NEW_TOKENS, timing=True, before_decode=collect))
+        acc["pending"] = True
+    end.record()
+    torch.cuda.synchronize(dev)
+    collect()
+    attn_ms, attn_n = acc["ms"], acc["n"]
+    barrier(world)
+    clocks = sampler.stop() if rank == 0 else None
+    launches = _lib.launch_count() - n0
+    ms_total = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms_total, world)
+    ms_per_step = ms_max / args.steps
+    tokens_all = sum_over_ranks(float(len(prompts) * NEW_TOKENS * args.steps), world)
+    value = tokens_all / (ms_max / 1e3)
+
+    # divergences: tracked row identical in every timed step and to its solo run
+    divergences = 0
+    if rank == 0:
+        for o in outs:
+            if not torch.equal(o[0], solo):
+                divergences += 1
+
+    # ---- end-to-end through the public API with host buffers ----
+    for _ in range(0 if args.skip_e2e else 2):   # warm the public path (graph captured on first use)
+        model.generate(prompts, NEW_TOKENS, "batch_invariant").cpu()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h2d = 0
+    d2h = 0
+    e_start.record()
+    for _ in range(0 if args.skip_e2e else args.steps):
+        res = model.generate(prompts, NEW_TOKENS, "batch_invariant")
+        host = res.cpu()
+        d2h = host.numel() * host.element_size()
+    e_end.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    h2d = eng.plan(prompts)["h2d_bytes"]
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+    e2e_value = None if args.skip_e2e else tokens_all / (e2e_ms / 1e3)
+
+    if rank != 0:
+        return 0
+
+    # ---- roofline of the dominant kernel (decode attention, HBM bound) ----
+    peaks, peak_kind = load_peaks()
+    lens = np.array([len(p) for p in prompts], dtype=np.int64)
+    H, D = MODEL["num_heads"], MODEL["head_dim"]
+    steps_dec = NEW_TOKENS - 1
+    kv_bytes = 0
+    for t in range(steps_dec):
+        kv_bytes += int((lens + t + 1).sum()) * H * D * 2 * 2  # K and V, bf16
+    qo_bytes = len(prompts) * H * D * 2 * 2
+    per_step_bytes = (kv_bytes + steps_dec * qo_bytes) * MODEL["num_layers"]
+    launches_per_step = steps_dec * MODEL["num_layers"]
+    avg_bytes = per_step_bytes / launches_per_step
+    avg_ms = attn_ms / max(attn_n, 1)
+    achieved = avg_bytes / (avg_ms / 1e3) / 1e9
+    roofline = {"kernel": "attn_kernel<bf16,64> (decode attention)", "bound": "hbm",
+                "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peak_kind,
+                "traffic": None, "avg_launch_us": round(avg_ms * 1e3, 2),
+                "algorithmic_bytes_per_launch": int(avg_bytes),
+                "share_of_step": round(attn_ms / args.steps / ms_per_step, 3)}
+
+    cpu, cpu_toks = (cpu_sample(cpu_sample_prompts(), 16, model) if world == 1 and not args.skip_cpu
+                     else (None, None))
+    parity = None
+    if cpu_toks is not None:
+        ours_small = model.generate(cpu_sample_prompts(), 16, "batch_invariant").cpu().numpy()
+        parity = {"oracle_token_match": float((ours_small == cpu_toks).mean()),
+                  "tracked_prefix_match": int(np.argmin(np.append(ours_small[0] == cpu_toks[0], False)))}
+
+    gemm = gemm_vs_cublas() if not args.skip_gemm else None
+
+    line = {
+        "metric": "BI decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random prompts, random-init weights)",
+        "config": {"workload": WORKLOAD_NAME, "global_batch": BATCH_PER_GPU * world,
+                   "new_tokens": NEW_TOKENS, "parallelism": "dp%d (request-sharded, no collective)" % world,
+                   "l2": "inputs larger than L2 (KV cache %.1f GB/GPU, weights 168 MB)"
+                         % (eng.k_cache[0].numel() * 2 * 2 * MODEL["num_layers"] / 1e9)},
+        "e2e": {"value": e2e_value and round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": int(launches),
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "divergences": divergences,
+        "parity": parity,
+        "gemm_vs_cublas": gemm,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    global NEW_TOKENS
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-gemm", action="store_true", help="skip the GEMM-vs-cuBLAS table")
+    ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--skip-e2e", action="store_true", help="skip the end-to-end public-API timing")
+    ap.add_argument("--new-tokens", type=int, default=NEW_TOKENS,
+                    help="tokens generated per prompt (the workload is 128; smaller only for profiling)")
+    args = ap.parse_args(argv)
+    NEW_TOKENS = args.new_tokens
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        return run_reference(args, rank, int(os.environ.get("WORLD_SIZE", "1")))
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        return run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

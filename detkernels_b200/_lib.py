@@ -141,6 +141,19 @@ def raise_on_device_error(device: int) -> None:
         raise DetKernelsError(code, "device status %d (detail 0x%x) on cuda:%d" % (code, detail, device))
 
 
+# ---- launch accounting (host side): every wrapper that launches one of this
+# library's kernels adds to it; captured CUDA graphs record the count at capture ----
+_launches = [0]
+
+
+def count_launch(n: int = 1) -> None:
+    _launches[0] += n
+
+
+def launch_count() -> int:
+    return _launches[0]
+
+
 # ---- torch glue ----
 def dtype_code(dtype) -> int:
     import torch

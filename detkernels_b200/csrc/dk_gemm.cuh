@@ -6,6 +6,11 @@
 //
 // C[M,N] = A[M,K] @ B[K,N], A and B row-major bf16/f16, f32 accumulation.
 //
+// When all M rows fit one 128-token tile, the activation TMA box covers only
+// ceil8(M) rows; the instruction still spans 128 token columns, and columns
+// beyond the box read stale shared memory.  Each output column depends only on
+// its own token row, and stale columns are never stored.
+//
 // Formulation ("swap-AB"): the tensor-core instruction computes
 //   D[n, m] = sum_k B[k, n] * A[m, k]
 // with the 128 weight columns of a tile on the UMMA M axis (B read MN-major,
@@ -69,6 +74,7 @@ struct Params {
   int group;                     // slices per work unit
   int n_tiles, m_tiles;
   int mode;
+  int a_rows;      // rows of the activation TMA box (128, or fewer when M fits one tile)
   void* c;
   int64_t ldc;
   float* ws;       // SPLIT/PARTIAL: partials [slice][M][N]; ATOMIC: [M][N]
@@ -168,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kb = 0; kb < nkb; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, kDetProdEmpty, abort_flag)) break;
             uint8_t* st = smem + stage * kStageBytes;
-            mbar_arrive_expect_tx(&full[stage], kStageBytes);
+            mbar_arrive_expect_tx(&full[stage], kWTileBytes + p.a_rows * kBK * 2);
             const int kk = k0 + kb * kBK;
             tma_load_2d(st, &tmB, &full[stage], nt * kTileN, kk);
             tma_load_2d(st + kWBoxBytes, &tmB, &full[stage], nt * kTileN + 64, kk);
@@ -342,14 +348,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool is_last = *last_flag != 0;
         if (is_last && n_ok) {
           __threadfence();
-          for (int i = 0; i < kEpiCols; ++i) {
-            const int m = m0 + i;
-            if (m >= p.M) break;
-            const float* src = p.ws + static_cast<int64_t>(m) * p.N + n;
-            float a = __ldcg(src);
+          const int rows = min(kEpiCols, p.M - m0);
+          // 4 rows x 8 slices of independent loads in flight per iteration
+          for (int i0 = 0; i0 < rows; i0 += 4) {
+            float part[4][kSlices];
 #pragma unroll
-            for (int s = 1; s < kSlices; ++s) a = __fadd_rn(a, __ldcg(src + s * MN));
-            C[static_cast<int64_t>(m) * p.ldc + n] = from_f32<T>(a);
+            for (int r = 0; r < 4; ++r) {
+              const float* src = p.ws + static_cast<int64_t>(m0 + min(i0 + r, rows - 1)) * p.N + n;
+#pragma unroll
+              for (int s = 0; s < kSlices; ++s) part[r][s] = __ldcg(src + s * MN);
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              if (i0 + r < rows) {
+                float a = part[r][0];
+#pragma unroll
+                for (int s = 1; s < kSlices; ++s) a = __fadd_rn(a, part[r][s]);
+                C[static_cast<int64_t>(m0 + i0 + r) * p.ldc + n] = from_f32<T>(a);
+              }
+            }
           }
         }
         // keep last_flag stable until every thread has read it

@@ -192,13 +192,36 @@ struct GemmPlan {
   size_t partials_off; // byte offset of the partials region
 };
 
-GemmPlan plan_invariant(int64_t M, int64_t N, int sms) {
+// Schedule choice (never changes the arithmetic): slices per work unit.  A
+// small cost model -- per-SM streaming of the unit's operand tiles in waves,
+// plus the L2 round trip of the f32 slice partials when slices are spread
+// over CTAs -- picks the cheapest of 8 (FOLD), 4, 2, 1 (SPLIT).
+int pick_group(int64_t M, int64_t N, int64_t K, int64_t tiles, int sms) {
+  const double kSmBytesPerUs = 100e3;   // sustained TMA bytes per SM per microsecond
+  const double kL2BytesPerUs = 10e6;    // L2 bytes per microsecond for the partial round trip
+  const int64_t kb_per_slice = ceil_div(slice_len_for(K, dk::gemm::kSlices), dk::gemm::kBK);
+  double best = 1e30;
+  int best_g = dk::gemm::kSlices;
+  for (int g = dk::gemm::kSlices; g >= 1; g /= 2) {
+    const int64_t units = tiles * (dk::gemm::kSlices / g);
+    const int64_t waves = ceil_div(units, sms);
+    const double load = static_cast<double>(waves) * g * kb_per_slice * dk::gemm::kStageBytes / kSmBytesPerUs;
+    const double part = (g < dk::gemm::kSlices) ? 2.0 * dk::gemm::kSlices * M * N * 4 / kL2BytesPerUs : 0.0;
+    const double t = load + part;
+    if (t < best * 0.97) {
+      best = t;
+      best_g = g;
+    }
+  }
+  return best_g;
+}
+
+GemmPlan plan_invariant(int64_t M, int64_t N, int64_t K, int sms) {
   GemmPlan pl{};
   pl.n_tiles = static_cast<int>(ceil_div(N, dk::gemm::kTileN));
   pl.m_tiles = static_cast<int>(ceil_div(M, dk::gemm::kTileM));
   const int64_t tiles = static_cast<int64_t>(pl.n_tiles) * pl.m_tiles;
-  int group = dk::gemm::kSlices;
-  while (group > 1 && tiles * (dk::gemm::kSlices / group) < sms) group /= 2;
+  const int group = pick_group(M, N, K, tiles, sms);
   pl.group = group;
   pl.mode = (group == dk::gemm::kSlices) ? dk::gemm::FOLD : dk::gemm::SPLIT;
   if (pl.mode == dk::gemm::SPLIT) {
@@ -226,13 +249,14 @@ int gemm_validate(const void* a, int64_t lda, const void* b, int64_t ldb, int64_
 
 int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb, dk::gemm::Params p,
                 cudaStream_t st, const char* what) {
+  p.a_rows = (p.m_tiles == 1) ? static_cast<int>(ceil_div(p.M, 8) * 8) : dk::gemm::kTileM;
   CUtensorMap tmB, tmA;
   const uint64_t dimsB[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K)};
   const uint64_t strB[1] = {static_cast<uint64_t>(ldb) * 2};
   const uint32_t boxB[2] = {64, static_cast<uint32_t>(dk::gemm::kBK)};
   const uint64_t dimsA[2] = {static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M)};
   const uint64_t strA[1] = {static_cast<uint64_t>(lda) * 2};
-  const uint32_t boxA[2] = {static_cast<uint32_t>(dk::gemm::kBK), static_cast<uint32_t>(dk::gemm::kTileM)};
+  const uint32_t boxA[2] = {static_cast<uint32_t>(dk::gemm::kBK), static_cast<uint32_t>(p.a_rows)};
   const CUtensorMapDataType dt = (dtype == DK_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   int rc = encode_map(&tmB, dt, 2, b, dimsB, strB, boxB, CU_TENSOR_MAP_SWIZZLE_128B, what);
   if (rc) return rc;
@@ -408,9 +432,8 @@ int dk_rmsnorm_batch_variant(const void* x, int64_t x_row_stride, const void* we
 
 // ---------------- matmul ----------------
 size_t dk_matmul_workspace_size(int64_t M, int64_t N, int64_t K) {
-  (void)K;
   if (M <= 0 || N <= 0) return 0;
-  return plan_invariant(M, N, sm_count(current_device())).ws_bytes;
+  return plan_invariant(M, N, K, sm_count(current_device())).ws_bytes;
 }
 
 size_t dk_matmul_variant_workspace_size(int64_t M, int64_t N) {
@@ -429,7 +452,7 @@ int dk_matmul_batch_invariant(const void* a, int64_t lda, const void* b, int64_t
   if (ldc < N) return fail(DK_ERR_INVALID_ARGUMENT, "%s: ldc < N", what);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (K == 0) return zero_output(c, ldc, M, N, 2, st);
-  const GemmPlan pl = plan_invariant(M, N, sm_count(current_device()));
+  const GemmPlan pl = plan_invariant(M, N, K, sm_count(current_device()));
   dk::gemm::Params p{};
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);

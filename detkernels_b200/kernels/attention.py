@@ -105,6 +105,7 @@ def attention_decode(q, k_cache, v_cache, kv_lens, *, scale=None, row_tiles=None
         _lib.dtype_code(q.dtype), workspace.data_ptr() if workspace is not None else None,
         workspace.numel() if workspace is not None else 0, stream)
     _lib.check(rc, "attention_batch_invariant")
+    _lib.count_launch()
     return out
 
 

@@ -78,6 +78,7 @@ def matmul_batch_invariant(a, b, block_m: int = 64, block_n: int = 64, block_k: 
         _lib.dtype_code(a.dtype), ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
         stream)
     _lib.check(rc, "matmul_batch_invariant")
+    _lib.count_launch()
     return c
 
 

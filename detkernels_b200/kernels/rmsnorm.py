@@ -60,6 +60,7 @@ def rmsnorm_batch_invariant(x, weight, eps: float = 1e-6):
         x2d.data_ptr(), x2d.stride(0), w.data_ptr(), out.data_ptr(), out.stride(0), n_rows, n_cols,
         _lib.dtype_code(x.dtype), _lib.dtype_code(w.dtype), float(eps), _lib.stream_ptr(x.device))
     _lib.check(rc, "rmsnorm_batch_invariant")
+    _lib.count_launch()
     return out.reshape(orig_shape)
 
 

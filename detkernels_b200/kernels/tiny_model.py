@@ -1,0 +1,505 @@
+"""Random-weight decode-only transformer over the batch-invariant kernels.
+
+Drop-in for the reference's ``kernels/tiny_model.py``:
+
+* ``TinyModelConfig`` (tiny_model.py:50-62) with the same fields and defaults,
+  plus keyword extensions: ``num_kv_heads`` (grouped KV heads), ``mlp``
+  (``"silu"``: the reference's ``silu(x W1) W2``; ``"swiglu"``:
+  ``(silu(x Wg) * x Wu) W2``) and ``dtype`` (the reference's float16 by default).
+* ``TinyModel.__init__`` (tiny_model.py:70-97) draws the weights in the
+  reference's order from a seeded generator on the model's device, so the same
+  config and seed give the same weights.
+* ``TinyModel.forward_step`` (tiny_model.py:99-140) and ``TinyModel.generate``
+  (tiny_model.py:142-157) keep the reference's signatures and semantics
+  (growing KV dicts, greedy argmax).  ``generate`` also accepts a list of
+  token-id lists as ragged prompts.
+* ``_KERNEL_SETS`` (tiny_model.py:36-47): ``batch_invariant``,
+  ``batch_variant``, plus ``reference`` (the eager torch formulas, any device).
+
+``DecodeEngine`` is the serving path used by ``generate`` for the invariant
+kernel set on CUDA: a preallocated (zeroed) KV cache, prompts prefilled as
+rows through the same per-row kernels (attention row tiles give exactly the
+bits of token-by-token decoding), fused QKV and gate/up weights (every output
+column is computed exactly as by the separate matmul), and the decode step
+captured once in a CUDA graph and replayed.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+from .attention import attention_batch_invariant, attention_batch_variant, attention_decode, attention_reference
+from .matmul import matmul_batch_invariant, matmul_batch_variant, matmul_reference
+from .rmsnorm import rmsnorm_batch_invariant, rmsnorm_batch_variant, rmsnorm_reference
+
+_KERNEL_SETS = {
+    "batch_invariant": {
+        "rmsnorm": rmsnorm_batch_invariant,
+        "matmul": matmul_batch_invariant,
+        "attention": attention_batch_invariant,
+    },
+    "batch_variant": {
+        "rmsnorm": rmsnorm_batch_variant,
+        "matmul": matmul_batch_variant,
+        "attention": attention_batch_variant,
+    },
+    "reference": {
+        "rmsnorm": rmsnorm_reference,
+        "matmul": matmul_reference,
+        "attention": attention_reference,
+    },
+}
+
+
+@dataclass
+class TinyModelConfig:
+    vocab_size: int = 256
+    num_layers: int = 4
+    num_heads: int = 4
+    head_dim: int = 32
+    mlp_hidden: int = 256
+    eps: float = 1e-6
+    seed: int = 0
+    num_kv_heads: Optional[int] = None
+    mlp: str = "silu"
+    dtype: str = "float16"
+
+    @property
+    def hidden_size(self) -> int:
+        return self.num_heads * self.head_dim
+
+    @property
+    def kv_heads(self) -> int:
+        return self.num_heads if self.num_kv_heads is None else self.num_kv_heads
+
+
+def _torch_dtype(name):
+    import torch
+    return {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32}[name]
+
+
+class TinyModel:
+    """Random-weight decode-only transformer (reference tiny_model.py:64-157)."""
+
+    def __init__(self, config: TinyModelConfig, device: str = "cuda"):
+        import torch
+
+        if config.mlp not in ("silu", "swiglu"):
+            raise ValueError("mlp must be 'silu' or 'swiglu'")
+        if config.num_heads % config.kv_heads != 0:
+            raise ValueError("num_heads must be a multiple of num_kv_heads")
+        self.config = config
+        self.device = device
+        self.dtype = _torch_dtype(config.dtype)
+
+        h = config.hidden_size
+        hkv = config.kv_heads * config.head_dim
+        g = torch.Generator(device=device).manual_seed(config.seed)
+
+        def randn(*shape):
+            return 0.02 * torch.randn(*shape, device=device, dtype=self.dtype, generator=g)
+
+        self.embed = randn(config.vocab_size, h)
+        self.layers = []
+        for _ in range(config.num_layers):
+            layer = {
+                "norm1_w": randn(h) + 1.0,
+                "w_q": randn(h, h),
+                "w_k": randn(h, hkv),
+                "w_v": randn(h, hkv),
+                "w_o": randn(h, h),
+                "norm2_w": randn(h) + 1.0,
+            }
+            if config.mlp == "swiglu":
+                layer["w_gate"] = randn(h, config.mlp_hidden)
+                layer["w_up"] = randn(h, config.mlp_hidden)
+            else:
+                layer["w_mlp1"] = randn(h, config.mlp_hidden)
+            layer["w_mlp2"] = randn(config.mlp_hidden, h)
+            self.layers.append(layer)
+        self.norm_f_w = randn(h) + 1.0
+        self.w_lm_head = randn(h, config.vocab_size)
+        self._engines = {}
+
+    # ---- fused weights for the serving path (same bits per output column) ----
+    def fused_layer_weights(self):
+        import torch
+
+        fused = []
+        for layer in self.layers:
+            f = {"norm1_w": layer["norm1_w"], "norm2_w": layer["norm2_w"], "w_o": layer["w_o"],
+                 "w_mlp2": layer["w_mlp2"],
+                 "w_qkv": torch.cat([layer["w_q"], layer["w_k"], layer["w_v"]], dim=1).contiguous()}
+            if self.config.mlp == "swiglu":
+                f["w_gu"] = torch.cat([layer["w_gate"], layer["w_up"]], dim=1).contiguous()
+            else:
+                f["w_mlp1"] = layer["w_mlp1"]
+            fused.append(f)
+        return fused
+
+    def _mlp(self, layer, xn, matmul):
+        import torch
+
+        if self.config.mlp == "swiglu":
+            gte = torch.nn.functional.silu(matmul(xn, layer["w_gate"]))
+            return matmul(gte * matmul(xn, layer["w_up"]), layer["w_mlp2"])
+        return matmul(torch.nn.functional.silu(matmul(xn, layer["w_mlp1"])), layer["w_mlp2"])
+
+    def forward_step(self, token_ids, kv_cache, kernel_set: str):
+        """One decode step: token_ids (B,) int64 -> next-token logits (B, vocab_size),
+        and the updated per-layer KV cache (list of {"k", "v"}: [B, H_kv, S, D])."""
+        import torch
+
+        fns = _KERNEL_SETS[kernel_set]
+        rmsnorm, matmul, attention = fns["rmsnorm"], fns["matmul"], fns["attention"]
+        cfg = self.config
+        B = token_ids.shape[0]
+        H, Hkv, D = cfg.num_heads, cfg.kv_heads, cfg.head_dim
+
+        x = self.embed[token_ids]
+        new_kv_cache = []
+        for i, layer in enumerate(self.layers):
+            residual = x
+            xn = rmsnorm(x, layer["norm1_w"], cfg.eps)
+            q = matmul(xn, layer["w_q"]).view(B, H, D)
+            k_new = matmul(xn, layer["w_k"]).view(B, Hkv, 1, D)
+            v_new = matmul(xn, layer["w_v"]).view(B, Hkv, 1, D)
+            prev = kv_cache[i]
+            if prev is None:
+                k_cache, v_cache = k_new, v_new
+            else:
+                k_cache = torch.cat([prev["k"], k_new], dim=2)
+                v_cache = torch.cat([prev["v"], v_new], dim=2)
+            new_kv_cache.append({"k": k_cache, "v": v_cache})
+            attn_out = attention(q, k_cache, v_cache).reshape(B, H * D)
+            x = residual + matmul(attn_out, layer["w_o"])
+            residual2 = x
+            x = residual2 + self._mlp(layer, rmsnorm(x, layer["norm2_w"], cfg.eps), matmul)
+        logits = matmul(rmsnorm(x, self.norm_f_w, cfg.eps), self.w_lm_head)
+        return logits, new_kv_cache
+
+    def generate(self, prompt_token_ids, n_steps: int, kernel_set: str):
+        """Greedy decoding.  prompt_token_ids: (B,) int64 start tokens (the
+        reference's form) or a list of B token-id lists (ragged prompts).
+        Returns (B, n_steps) generated token ids."""
+        import torch
+
+        ragged = isinstance(prompt_token_ids, (list, tuple))
+        if kernel_set == "batch_invariant" and str(self.device).startswith("cuda"):
+            prompts = ([list(map(int, p)) for p in prompt_token_ids] if ragged
+                       else [[int(t)] for t in prompt_token_ids.tolist()])
+            cap = max(len(p) for p in prompts) + n_steps
+            eng = self.engine(len(prompts), cap)
+            return eng.generate(prompts, n_steps)
+        if ragged:
+            return self._generate_ragged_eager(prompt_token_ids, n_steps, kernel_set)
+        kv_cache = [None] * self.config.num_layers
+        current = prompt_token_ids
+        generated = []
+        for _ in range(n_steps):
+            logits, kv_cache = self.forward_step(current, kv_cache, kernel_set)
+            current = logits.argmax(dim=-1)
+            generated.append(current)
+        return torch.stack(generated, dim=1)
+
+    def _generate_ragged_eager(self, prompts, n_steps, kernel_set):
+        """Ragged prompts on the eager path: each sequence is decoded alone."""
+        import torch
+
+        outs = []
+        for p in prompts:
+            kv_cache = [None] * self.config.num_layers
+            ids = torch.tensor(list(p), device=self.device, dtype=torch.long)
+            logits = None
+            for t in range(len(p)):
+                logits, kv_cache = self.forward_step(ids[t:t + 1], kv_cache, kernel_set)
+            seq = []
+            cur = logits.argmax(dim=-1)
+            for s in range(n_steps):
+                seq.append(cur)
+                if s + 1 < n_steps:
+                    logits, kv_cache = self.forward_step(cur, kv_cache, kernel_set)
+                    cur = logits.argmax(dim=-1)
+            outs.append(torch.cat(seq))
+        return torch.stack(outs)
+
+    def engine(self, max_batch: int, max_seq_len: int, use_graph: bool = True) -> "DecodeEngine":
+        """A cached DecodeEngine whose capacity covers (max_batch, max_seq_len)."""
+        for (b, s, g), eng in self._engines.items():
+            if b >= max_batch and s >= max_seq_len and g == use_graph:
+                return eng
+        eng = DecodeEngine(self, max_batch, max_seq_len, use_graph=use_graph)
+        self._engines[(max_batch, max_seq_len, use_graph)] = eng
+        return eng
+
+
+class DecodeEngine:
+    """Batch-invariant serving loop for a TinyModel on one GPU.
+
+    KV cache: per layer [max_batch, H_kv, max_seq_len, D] in the model dtype,
+    zero-initialised.  A sequence's arithmetic never depends on its batch: every
+    op is per-row, prefill rows of one sequence share attention tiles that
+    reproduce decode-row bits, and the decode graph has a fixed shape (rows
+    beyond the live batch are computed and ignored)."""
+
+    def __init__(self, model: TinyModel, max_batch: int, max_seq_len: int, use_graph: bool = True):
+        import torch
+
+        from .. import _lib
+
+        self.model = model
+        cfg = model.config
+        self.cfg = cfg
+        self.device = torch.device(model.device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.dtype = model.dtype
+        self.B = int(max_batch)
+        self.S = int(max_seq_len)
+        self.H, self.Hkv, self.D = cfg.num_heads, cfg.kv_heads, cfg.head_dim
+        self.h = cfg.hidden_size
+        self.use_graph = use_graph
+        self.layers = model.fused_layer_weights()
+        dev, dt = self.device, self.dtype
+        self.k_cache = [torch.zeros(self.B, self.Hkv, self.S, self.D, device=dev, dtype=dt)
+                        for _ in range(cfg.num_layers)]
+        self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
+        # decode-step state
+        self.tokens = torch.zeros(self.B, dtype=torch.long, device=dev)
+        self.kv_lens = torch.zeros(self.B, dtype=torch.int32, device=dev)
+        self.rows = torch.arange(self.B, device=dev)
+        self._graphs = {}
+        self._last_events = None
+        # explicit scratch so captured graphs never allocate
+        self._lib = _lib
+        lib = _lib.load()
+        qkv_n = (self.H + 2 * self.Hkv) * self.D
+        gemm_shapes = [(self.B, qkv_n, self.h), (self.B, self.h, self.h), (self.B, self.h, cfg.mlp_hidden),
+                       (self.B, cfg.vocab_size, self.h),
+                       (self.B, 2 * cfg.mlp_hidden if cfg.mlp == "swiglu" else cfg.mlp_hidden, self.h)]
+        g_ws = max(lib.dk_matmul_workspace_size(m, n, k) for (m, n, k) in gemm_shapes)
+        a_ws = lib.dk_attention_workspace_size(self.B, 1, self.H, self.Hkv, self.D, self.S)
+        self.gemm_ws = torch.zeros(max(g_ws, 1), dtype=torch.uint8, device=dev)
+        self.attn_ws = torch.zeros(max(a_ws, 1), dtype=torch.uint8, device=dev)
+
+    # ---------------- building blocks (all per-row) ----------------
+    def _mm(self, x, w, ws=None):
+        return _matmul_ws(x, w, self.gemm_ws if ws is None else ws)
+
+    def _mlp(self, layer, xn):
+        import torch
+
+        F = self.cfg.mlp_hidden
+        if self.cfg.mlp == "swiglu":
+            gu = self._mm(xn, layer["w_gu"])
+            h = torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]
+        else:
+            h = torch.nn.functional.silu(self._mm(xn, layer["w_mlp1"]))
+        return self._mm(h, layer["w_mlp2"])
+
+    def _layer(self, li, layer, x, write_rows, write_pos, q_lens, row_tiles, max_len, attn_ws, events=None):
+        """One transformer block over R rows.  K/V of every row are written to
+        (write_rows, write_pos) before attention reads them."""
+        cfg = self.cfg
+        R = x.shape[0]
+        H, Hkv, D = self.H, self.Hkv, self.D
+        xn = rmsnorm_batch_invariant(x, layer["norm1_w"], cfg.eps)
+        qkv = self._mm(xn, layer["w_qkv"])
+        q = qkv[:, :H * D].view(R, H, D)
+        k = qkv[:, H * D:(H + Hkv) * D].view(R, Hkv, D)
+        v = qkv[:, (H + Hkv) * D:].view(R, Hkv, D)
+        self.k_cache[li][write_rows, :, write_pos, :] = k
+        self.v_cache[li][write_rows, :, write_pos, :] = v
+        if events is not None:
+            events[0].record()
+        attn = attention_decode(q, self.k_cache[li], self.v_cache[li], q_lens, row_tiles=row_tiles,
+                                max_kv_len=max_len, workspace=attn_ws)
+        if events is not None:
+            events[1].record()
+        x = x + self._mm(attn.reshape(R, H * D), layer["w_o"])
+        return x + self._mlp(layer, rmsnorm_batch_invariant(x, layer["norm2_w"], cfg.eps))
+
+    def _logits(self, x):
+        xn = rmsnorm_batch_invariant(x, self.model.norm_f_w, self.cfg.eps)
+        return self._mm(xn, self.model.w_lm_head)
+
+    # ---------------- prefill ----------------
+    def plan(self, prompts: Sequence[Sequence[int]]):
+        """Device-side description of a prefill: every prompt token is a row."""
+        import torch
+
+        dev = self.device
+        B = len(prompts)
+        assert 0 < B <= self.B, "batch exceeds engine capacity"
+        G = self.H // self.Hkv
+        rows_per_tile = 16 // G
+        seq_idx, pos_idx, tiles, last = [], [], [], []
+        for b, p in enumerate(prompts):
+            assert 0 < len(p) <= self.S, "prompt longer than engine capacity"
+            for t0 in range(0, len(p), rows_per_tile):
+                n = min(rows_per_tile, len(p) - t0)
+                tiles.append((len(seq_idx), n, b))
+                seq_idx += [b] * n
+                pos_idx += list(range(t0, t0 + n))
+            last.append(len(seq_idx) - 1)
+        host = {
+            "tok": torch.tensor([t for p in prompts for t in p], dtype=torch.long),
+            "rows": torch.tensor(seq_idx, dtype=torch.long),
+            "pos": torch.tensor(pos_idx, dtype=torch.long),
+            "tiles": torch.tensor(tiles, dtype=torch.int32),
+            "last": torch.tensor(last, dtype=torch.long),
+            "lens": torch.tensor([len(p) for p in prompts], dtype=torch.int32),
+        }
+        plan = {k: v.pin_memory().to(dev, non_blocking=True) for k, v in host.items()}
+        plan["q_lens"] = (plan["pos"] + 1).to(torch.int32)
+        plan["B"] = B
+        plan["max_len"] = max(len(p) for p in prompts)
+        plan["h2d_bytes"] = sum(v.numel() * v.element_size() for v in host.values())
+        lib = self._lib.load()
+        R = host["tok"].numel()
+        a_ws = lib.dk_attention_workspace_size(len(tiles), 2, self.H, self.Hkv, self.D, plan["max_len"])
+        g_ws = max(lib.dk_matmul_workspace_size(R, n, k) for (n, k) in [
+            ((self.H + 2 * self.Hkv) * self.D, self.h), (self.h, self.h), (self.h, self.cfg.mlp_hidden),
+            (2 * self.cfg.mlp_hidden, self.h), (self.cfg.mlp_hidden, self.h)])
+        plan["attn_ws"] = torch.zeros(max(a_ws, 1), dtype=torch.uint8, device=dev)
+        plan["gemm_ws"] = torch.zeros(max(g_ws, 1), dtype=torch.uint8, device=dev)
+        return plan
+
+    def prefill(self, plan):
+        """Run a planned prefill; returns logits of each prompt's last token and
+        leaves the cache and kv_lens ready for decoding."""
+        saved = self.gemm_ws
+        self.gemm_ws = plan["gemm_ws"]
+        try:
+            x = self.model.embed[plan["tok"]]
+            for li, layer in enumerate(self.layers):
+                x = self._layer(li, layer, x, plan["rows"], plan["pos"], plan["q_lens"], plan["tiles"],
+                                plan["max_len"], plan["attn_ws"])
+            logits = self._logits(x[plan["last"]])
+        finally:
+            self.gemm_ws = saved
+        self.kv_lens.zero_()
+        self.kv_lens[:plan["B"]] = plan["lens"]
+        return logits
+
+    # ---------------- decode ----------------
+    def _decode_step(self, max_len, events=None):
+        """tokens -> next tokens for all rows; K/V written at kv_lens, then kv_lens += 1.
+        max_len bounds every row's length after this step (sizes the attention grid)."""
+        import torch
+
+        x = self.model.embed[self.tokens]
+        pos = self.kv_lens.long()
+        q_lens = self.kv_lens + 1
+        for li, layer in enumerate(self.layers):
+            if events is not None:
+                ev = (torch.cuda.Event(enable_timing=True, external=True),
+                      torch.cuda.Event(enable_timing=True, external=True))
+                events.append(ev)
+                x = self._layer(li, layer, x, self.rows, pos, q_lens, None, max_len, self.attn_ws, ev)
+            else:
+                x = self._layer(li, layer, x, self.rows, pos, q_lens, None, max_len, self.attn_ws)
+        nxt = self._logits(x).argmax(dim=-1)
+        self.tokens.copy_(nxt)
+        self.kv_lens.add_(1)
+        return nxt
+
+    def _capture(self, n_steps, start_len, timing):
+        """Capture n_steps decode steps (one graph) starting from rows of length <= start_len."""
+        import torch
+
+        out = torch.empty((n_steps, self.B), dtype=torch.long, device=self.device)
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        saved = (self.tokens.clone(), self.kv_lens.clone())
+        with torch.cuda.stream(s):   # warm-up: lazy loads and tensor-map encoding
+            self._decode_step(start_len + 1)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.tokens.copy_(saved[0])
+        self.kv_lens.copy_(saved[1])
+        events = [] if timing else None
+        g = torch.cuda.CUDAGraph()
+        n0 = self._lib.launch_count()
+        with torch.cuda.graph(g):
+            for t in range(n_steps):
+                out[t].copy_(self._decode_step(min(start_len + t + 1, self.S), events))
+        n_graph = self._lib.launch_count() - n0
+        self._lib.count_launch(-n_graph)  # recorded, not executed; counted at each replay
+        return g, out, events, n_graph
+
+    def decode(self, n_steps: int, start_len: Optional[int] = None, timing: bool = False):
+        """Run n_steps decode steps from the current tokens/kv_lens; returns [n_steps, B]
+        (device).  start_len bounds the current kv_lens (defaults to the capacity).
+        With timing=True, per-launch attention durations of the run are available
+        from attention_times_ms() afterwards."""
+        import torch
+
+        if n_steps <= 0:
+            return torch.empty((0, self.B), dtype=torch.long, device=self.device)
+        if start_len is None:
+            start_len = self.S - n_steps
+        if not self.use_graph:
+            out = torch.empty((n_steps, self.B), dtype=torch.long, device=self.device)
+            for t in range(n_steps):
+                out[t].copy_(self._decode_step(min(start_len + t + 1, self.S)))
+            return out
+        key = (n_steps, start_len, timing)
+        if key not in self._graphs:
+            self._graphs[key] = self._capture(n_steps, start_len, timing)
+        g, out, events, n_graph = self._graphs[key]
+        g.replay()
+        self._lib.count_launch(n_graph)
+        self._last_events = events
+        return out
+
+    def attention_times_ms(self):
+        """Durations (ms) of every attention launch of the last timed decode.
+        Waits for that decode's last event only (not the whole device)."""
+        evs = self._last_events or []
+        if not evs:
+            return []
+        evs[-1][1].synchronize()
+        return [a.elapsed_time(b) for a, b in evs]
+
+    def run(self, plan, n_steps: int, timing: bool = False, before_decode=None):
+        """Prefill + greedy decode; returns [B, n_steps] generated ids (device).
+        before_decode (optional) is called on the host after the prefill has been
+        queued and before the decode graph is launched."""
+        import torch
+
+        B = plan["B"]
+        if n_steps <= 0:
+            return torch.empty((B, 0), dtype=torch.long, device=self.device)
+        if plan["max_len"] + n_steps > self.S:
+            raise ValueError("prompt + n_steps exceeds the engine's max_seq_len")
+        first = self.prefill(plan).argmax(dim=-1)
+        self.tokens.zero_()
+        self.tokens[:B] = first
+        if before_decode is not None:
+            before_decode()
+        rest = self.decode(n_steps - 1, start_len=plan["max_len"], timing=timing)
+        return torch.cat([first[:, None], rest[:, :B].t()], dim=1)
+
+    def generate(self, prompts: Sequence[Sequence[int]], n_steps: int):
+        """Greedy decode of n_steps tokens after each prompt; returns [B, n_steps] (device)."""
+        return self.run(self.plan(prompts), n_steps)
+
+
+def _matmul_ws(x, w, ws):
+    """matmul_batch_invariant with a caller-owned workspace (no allocation, graph-safe)."""
+    import torch
+
+    from .. import _lib
+    from .matmul import _tma_ready
+
+    M, K = x.shape
+    N = w.shape[1]
+    c = torch.empty((M, N), device=x.device, dtype=x.dtype)
+    a = _tma_ready(x)
+    lib = _lib.load()
+    rc = lib.dk_matmul_batch_invariant(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), c.data_ptr(),
+                                       c.stride(0), M, N, K, _lib.dtype_code(x.dtype), ws.data_ptr(), ws.numel(),
+                                       _lib.stream_ptr(x.device))
+    _lib.check(rc, "matmul_batch_invariant")
+    _lib.count_launch()
+    return c
