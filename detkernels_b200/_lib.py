@@ -61,6 +61,10 @@ SIGNATURES = {
     "dk_attention_batch_invariant": (_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64,
                                             _i64, _c_void_p, _i64, _i64, _c_void_p, _i32, _c_void_p, _i32, _i32,
                                             _i32, _i32, _i32, _i32, _f32, _int, _c_void_p, _size, _c_void_p]),
+    "dk_attention_noalloc_scratch_limit": (_size, []),
+    "dk_attention_batch_invariant_noalloc": (_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64,
+                                                    _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i32, _c_void_p,
+                                                    _i32, _i32, _i32, _i32, _i32, _i32, _f32, _int, _c_void_p]),
     "dk_attention_variant_workspace_size": (_size, [_i32, _i32, _i32]),
     "dk_attention_batch_variant": (_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p,
                                           _i64, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _int, _c_void_p, _size,

@@ -341,6 +341,34 @@ int attn_launch(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Pa
 
 }  // namespace
 
+// Fixed scratch for dk_attention_batch_invariant_noalloc (32 MiB per device, zero at load).
+constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(32) << 20;
+static __device__ __align__(256) unsigned char dk_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[kMaxDevices] = {nullptr};
+
+// Device address of dk_noalloc_scratch on the current device, looked up on the first call
+// per device (with that device current) and cached.
+int noalloc_scratch(void** out, const char* what) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return fail(DK_ERR_UNSUPPORTED, "%s: device %d out of range", what, dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, dk_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(DK_ERR_CUDA, "%s: cudaGetSymbolAddress failed: %s", what, cudaGetErrorString(e));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return DK_OK;
+}
+
+}  // namespace
+
 // =====================================================================================
 extern "C" {
 
@@ -725,6 +753,49 @@ int dk_attention_batch_variant(const void* q, int64_t q_stride_b, int64_t q_stri
   }
 #undef DK_VAR_LAUNCH
   return check_launch(what);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Decode attention without a caller workspace.  Its scratch is a fixed-size array in device
+// global memory owned by this library image: each GPU that loads the library holds it until
+// the process exits.  In host code the array's name is only a host-side placeholder, so its
+// device address is looked up once per device with cudaGetSymbolAddress and cached.
+// ---------------------------------------------------------------------------------------------
+size_t dk_attention_noalloc_scratch_limit(void) { return kNoAllocScratchBytes; }
+
+int dk_attention_batch_invariant_noalloc(const void* q, int64_t q_stride_row, int64_t q_stride_head, const void* k,
+                                         const void* v, int64_t kv_stride_seq, int64_t kv_stride_head,
+                                         int64_t kv_stride_tok, int64_t kv_n_seq, int64_t kv_capacity, void* out,
+                                         int64_t out_stride_row, int64_t out_stride_head, const int32_t* kv_lens,
+                                         int32_t uniform_kv_len, const int32_t* row_tiles, int32_t n_tiles,
+                                         int32_t n_rows, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
+                                         int32_t max_kv_len, float scale, int dtype, void* stream) {
+  const char* what = "attention_batch_invariant_noalloc";
+  const int32_t tiles = row_tiles ? n_tiles : n_rows;
+  const size_t need = dk_attention_workspace_size(tiles, row_tiles ? 2 : 1, n_q_heads, n_kv_heads, head_dim,
+                                                  max_kv_len);
+  if (need > kNoAllocScratchBytes)
+    return fail(DK_ERR_WORKSPACE,
+                "%s: this call needs %zu bytes of scratch but the built-in scratch holds %zu; use "
+                "dk_attention_batch_invariant with a caller workspace (or fewer rows / a shorter max_kv_len)",
+                what, need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (need > 0) {
+    int rc = noalloc_scratch(&scratch, what);
+    if (rc) return rc;
+    // The arrival counters must start at zero; the previous call on this device may have left
+    // them non-zero if it stopped early.  Only the counters this call uses are cleared.
+    const size_t counter_bytes = static_cast<size_t>(tiles) * static_cast<size_t>(n_kv_heads) * sizeof(int32_t);
+    if (counter_bytes > kCounterBytes)
+      return fail(DK_ERR_INVALID_ARGUMENT, "%s: too many tiles x kv heads for the counter area", what);
+    cudaError_t e = cudaMemsetAsync(scratch, 0, counter_bytes, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(DK_ERR_CUDA, "%s: clearing counters: %s", what, cudaGetErrorString(e));
+  }
+  return dk_attention_batch_invariant(q, q_stride_row, q_stride_head, k, v, kv_stride_seq, kv_stride_head,
+                                      kv_stride_tok, kv_n_seq, kv_capacity, out, out_stride_row, out_stride_head,
+                                      kv_lens, uniform_kv_len, row_tiles, n_tiles, n_rows, n_q_heads, n_kv_heads,
+                                      head_dim, max_kv_len, scale, dtype, scratch,
+                                      scratch ? kNoAllocScratchBytes : 0, stream);
 }
 
 }  // extern "C"

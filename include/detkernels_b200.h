@@ -158,6 +158,28 @@ int dk_attention_batch_variant(const void* q, int64_t q_stride_b, int64_t q_stri
                                int32_t seq_len, int32_t head_dim, float scale, int32_t split_s, int dtype,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- decode attention for callers that cannot allocate device memory ----
+ * No counterpart in the reference.  Some callers cannot hand this library a workspace: code that
+ * runs inside another runtime's allocator or memory-pool callbacks, plugins whose host owns every
+ * device allocation, or paths where a cudaMalloc would synchronise the device at the wrong time.
+ * This entry point takes the same arguments as dk_attention_batch_invariant minus the workspace,
+ * and produces the same bits.  Its scratch is a 32 MiB array in device memory that belongs to the
+ * library (dk_attention_noalloc_scratch_limit() returns the size): every GPU that loads the library
+ * keeps it until the process exits.  Calls whose multi-split scratch would exceed it are rejected
+ * with DK_ERR_WORKSPACE.  It never allocates: the first call on a device looks up the array's
+ * device address with that device current (cudaGetSymbolAddress) and caches it, so make that first
+ * call before any stream capture on the device.  Each call clears the arrival counters it uses on
+ * `stream`.  All calls share the one array, so calls on one device that may overlap on the GPU (for
+ * example on different streams without ordering) race and give wrong results; order them. */
+size_t dk_attention_noalloc_scratch_limit(void);
+int dk_attention_batch_invariant_noalloc(const void* q, int64_t q_stride_row, int64_t q_stride_head, const void* k,
+                                         const void* v, int64_t kv_stride_seq, int64_t kv_stride_head,
+                                         int64_t kv_stride_tok, int64_t kv_n_seq, int64_t kv_capacity, void* out,
+                                         int64_t out_stride_row, int64_t out_stride_head, const int32_t* kv_lens,
+                                         int32_t uniform_kv_len, const int32_t* row_tiles, int32_t n_tiles,
+                                         int32_t n_rows, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
+                                         int32_t max_kv_len, float scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
