@@ -17,7 +17,7 @@ Shapes: q [B, H, D]; k, v [B, H_kv, S, D]; out like q.
 """
 from __future__ import annotations
 
-from .. import _lib
+from detkernels_b200 import _lib
 
 KV_SPLIT = _lib.ATTN_KV_SPLIT
 

@@ -19,7 +19,7 @@ A and B must be bf16 or f16 (same dtype); the output has a's dtype.
 """
 from __future__ import annotations
 
-from .. import _lib
+from detkernels_b200 import _lib
 
 K_SLICES = _lib.MATMUL_K_SLICES
 

@@ -17,7 +17,7 @@ The CUDA ops raise if the library is not built; there is no CPU fallback.
 """
 from __future__ import annotations
 
-from .. import _lib
+from detkernels_b200 import _lib
 
 
 def rmsnorm_reference(x, weight, eps: float = 1e-6):

@@ -245,7 +245,7 @@ class DecodeEngine:
     def __init__(self, model: TinyModel, max_batch: int, max_seq_len: int, use_graph: bool = True):
         import torch
 
-        from .. import _lib
+        from detkernels_b200 import _lib
 
         self.model = model
         cfg = model.config
@@ -489,7 +489,7 @@ def _matmul_ws(x, w, ws):
     """matmul_batch_invariant with a caller-owned workspace (no allocation, graph-safe)."""
     import torch
 
-    from .. import _lib
+    from detkernels_b200 import _lib
     from .matmul import _tma_ready
 
     M, K = x.shape
