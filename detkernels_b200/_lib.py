@@ -53,7 +53,7 @@ SIGNATURES = {
                                          _c_void_p, _size, _c_void_p]),
     "dk_matmul_slice_partials": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _int, _int,
                                         _int, _c_void_p]),
-    "dk_matmul_fold_slices": (_int, [_c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p]),
+    "dk_matmul_fold_slices": (_int, [_c_void_p, _int, _c_void_p, _i64, _i64, _i64, _int, _c_void_p]),
     "dk_matmul_variant_workspace_size": (_size, [_i64, _i64]),
     "dk_matmul_batch_variant": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _i64, _int,
                                        _int, _int, _c_void_p, _size, _c_void_p]),

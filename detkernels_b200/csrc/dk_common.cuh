@@ -119,6 +119,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int de
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch: kernels of this library may start while the
+// previous kernel on the stream is still finishing.  Every thread waits for the
+// previous grid (and its memory) before its first global-memory access, and a
+// CTA signals early that the next grid may begin its own launch.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ---------------------------------------------------------------------------
 // TMA
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {

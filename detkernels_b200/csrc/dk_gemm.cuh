@@ -6,40 +6,47 @@
 //
 // C[M,N] = A[M,K] @ B[K,N], A and B row-major bf16/f16, f32 accumulation.
 //
-// When all M rows fit one 128-token tile, the activation TMA box covers only
-// ceil8(M) rows; the instruction still spans 128 token columns, and columns
-// beyond the box read stale shared memory.  Each output column depends only on
-// its own token row, and stale columns are never stored.
-//
 // Formulation ("swap-AB"): the tensor-core instruction computes
 //   D[n, m] = sum_k B[k, n] * A[m, k]
 // with the 128 weight columns of a tile on the UMMA M axis (B read MN-major,
 // straight from its row-major [K, N] layout) and 128 tokens on the UMMA N axis
 // (A read K-major).  The tile shape (128 x 128 x 16 per instruction) is the
-// same for every M.
+// same for every M.  When all M rows fit one 128-token tile, the activation
+// TMA box covers only ceil8(M) rows; the instruction still spans 128 token
+// columns and columns beyond the box read stale shared memory.  Each output
+// column depends only on its own token row, and stale columns are never stored.
 //
 // Fixed reduction structure (the definition of the output bits):
 //   * K is cut into DK_MATMUL_K_SLICES = 8 slices of L = ceil16(ceil(K/8))
 //     elements; slice s covers [s*L, min((s+1)*L, K)).
 //   * Slice s is accumulated from zero in its own TMEM accumulator by
-//     tcgen05.mma steps of 16 K-elements in ascending K order.
-//   * The 8 f32 partials are folded in slice order ((p0 + p1) + p2) + ... + p7,
+//     tcgen05.mma steps of 16 K-elements in ascending K order: partial p_s.
+//   * The partials are summed in f32 along a fixed binary tree,
+//       ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)),
 //     then rounded to the output dtype (round to nearest even).
 // Nothing in that structure depends on M, N or the schedule, so a row's output
-// bits do not depend on the batch.  Only the schedule does:
-//   * FOLD:    a work unit = one output tile x all 8 slices; the epilogue warps
-//              fold each partial into a third TMEM buffer (tcgen05.ld / add /
-//              tcgen05.st), with the two accumulators double-buffered so slice
-//              s+1 is multiplied while slice s is drained.  Used when there are
-//              at least as many output tiles as SMs.
-//   * SPLIT:   a work unit = one output tile x a group of 1/2/4 slices; every
-//              partial goes to the workspace and the CTA that finishes a tile
-//              last (atomic arrival counter, no spinning) folds all 8 in slice
-//              order.  Used for small M to fill the GPU with K-parallel work.
-//   * PARTIAL: slices [slice_begin, slice_end) only, partials written out
-//              (row-parallel tensor parallelism).
+// bits do not depend on the batch.  The tree makes every aligned group of 1, 2,
+// 4 or 8 slices a subtree, so a group can be summed on its own and contribute
+// ONE partial; only the schedule decides where the groups are summed:
+//   * FOLD:    a work unit = one output tile x all 8 slices, summed in TMEM.
+//   * SPLIT:   a work unit = one output tile x an aligned group of 1, 2 or 4
+//              slices; each unit writes its subtree sum to the workspace and a
+//              second, fully parallel kernel (fold_groups_kernel, launched as a
+//              programmatic dependent of this one) adds the 8/g subtree sums
+//              along the upper tree levels.
+//   * PARTIAL: one aligned slice group per launch, its subtree sum written out
+//              (row-parallel tensor parallelism: a rank per group).
 //   * ATOMIC:  the deliberately batch-variant twin: split_k chunks added with
 //              f32 atomics (scheduler-dependent order).
+//
+// Accumulators: TMEM holds 4 slots of 128 columns.  Slice i of a unit is
+// multiplied into slot (kSlotTable[i] + unit_ordinal * step(g)) mod 4; the
+// epilogue keeps the tree's pending left operands in their slots, adds right
+// operands into them (tcgen05.ld / add / tcgen05.st) and releases every slot it
+// consumed.  The table guarantees that a slot's previous value is always
+// released by the epilogue of an EARLIER slice, so the MMA issuer never waits on
+// work that depends on itself, and with one exception per 8-slice unit it never
+// waits on the epilogue of the slice just before.
 #pragma once
 
 #include "dk_common.cuh"
@@ -51,19 +58,44 @@ constexpr int kTileN = 128;  // weight columns per tile (UMMA M)
 constexpr int kTileM = 128;  // tokens per tile (UMMA N)
 constexpr int kBK = 64;      // K per pipeline stage: one 128-byte swizzle row of bf16
 constexpr int kUK = 16;      // K per tcgen05.mma, kind::f16
-constexpr int kStages = 6;
+constexpr int kMaxStages = 16;   // ring depth is chosen per launch from the stage size
 constexpr int kSlices = DK_MATMUL_K_SLICES;
 constexpr int kWBoxBytes = 64 * kBK * 2;          // 64 columns x 64 k
 constexpr int kWTileBytes = 2 * kWBoxBytes;       // 128 columns x 64 k
 constexpr int kATileBytes = kTileM * kBK * 2;     // 128 tokens x 64 k
-constexpr int kStageBytes = kWTileBytes + kATileBytes;
 constexpr int kEpiWarps = 8;                      // two warps per TMEM lane quarter
 constexpr int kEpiThreads = 32 * kEpiWarps;
-constexpr int kEpiCols = kTileM / 2;              // token columns folded per epilogue thread
+constexpr int kEpiCols = kTileM / 2;              // token columns handled per epilogue thread
 constexpr int kThreads = 64 + kEpiThreads;        // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr int kTmemCols = 512;                    // two 128-column f32 accumulators + fold buffer
-constexpr int kSumCol = 2 * kTileM;               // TMEM column of the running slice fold
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kSlots = 4;
+constexpr int kTmemCols = kSlots * kTileM;        // 512: the whole tensor memory of the SM
+constexpr int kBarrierBytes = 512;
+constexpr int kSmemBytes = 232448;               // the sm_100 per-CTA maximum
+constexpr int kRingBytes = kSmemBytes - 1024 /*align*/ - kBarrierBytes;
+
+// Stage size for an activation box of a_rows rows: 16 KB of weights + a_rows x 128 B,
+// rounded up to the 1 KB swizzle period.  The MMA always reads 128 token rows
+// (16 KB) from a stage's activation region, i.e. up to (128 - a_rows) x 128 B
+// past the loaded rows: into the next stage (stale data, feeding columns that
+// are never stored) and, after the last stage, into a guard area kept free at
+// the end of the ring so that every read stays inside the CTA's shared memory.
+__host__ __device__ __forceinline__ int stage_bytes_for(int a_rows) {
+  return ((kWTileBytes + a_rows * kBK * 2 + 1023) / 1024) * 1024;
+}
+__host__ __device__ __forceinline__ int overhang_bytes_for(int a_rows) { return (kTileM - a_rows) * kBK * 2; }
+__host__ __device__ __forceinline__ int stages_for(int a_rows) {
+  const int n = (kRingBytes - overhang_bytes_for(a_rows)) / stage_bytes_for(a_rows);
+  return n < kMaxStages ? n : kMaxStages;
+}
+
+// kSlotTable[i] for i = 0..7 packed 2 bits each: {0, 1, 2, 1, 3, 1, 2, 1}.
+constexpr uint32_t kSlotTable = 0u | (1u << 2) | (2u << 4) | (1u << 6) | (3u << 8) | (1u << 10) | (2u << 12) |
+                                (1u << 14);
+
+__host__ __device__ __forceinline__ int slot_of(int i, int unit_ordinal, int group) {
+  const int step = (group == 2) ? 2 : (group == 4 ? 3 : 1);
+  return (static_cast<int>((kSlotTable >> (2 * i)) & 3u) + unit_ordinal * step) & 3;
+}
 
 enum Mode : int { FOLD = 0, SPLIT = 1, PARTIAL = 2, ATOMIC = 3 };
 
@@ -71,23 +103,21 @@ struct Params {
   int M, N, K;
   int slice_len;                 // elements per slice (multiple of 16)
   int slice_begin, slice_end;    // slices computed by this launch
-  int group;                     // slices per work unit
+  int group;                     // slices per work unit (aligned group, power of two)
   int n_tiles, m_tiles;
   int mode;
   int a_rows;      // rows of the activation TMA box (128, or fewer when M fits one tile)
   void* c;
   int64_t ldc;
-  float* ws;       // SPLIT/PARTIAL: partials [slice][M][N]; ATOMIC: [M][N]
-  int* counters;   // SPLIT: one arrival counter per output tile
+  float* ws;       // SPLIT: subtree sums [8/g][M][N]; PARTIAL: [M][N]; ATOMIC: [M][N]
 };
 
 // Detail codes recorded with a timeout (which wait expired).
 enum : int {
   kDetProdEmpty = 0x100,
-  kDetMmaAccEmpty = 0x101,
+  kDetMmaSlotFree = 0x101,
   kDetMmaFull = 0x102,
-  kDetEpiAccFull = 0x103,
-  kDetEpiSync = 0x104,
+  kDetEpiSlotFull = 0x103,
   kDetDrain = 0x105,
 };
 
@@ -97,14 +127,39 @@ __device__ __forceinline__ void slice_bounds(const Params& p, int s, int& k0, in
   if (k1 < k0) k1 = k0;
 }
 
-// Bounded barrier among the epilogue threads (an mbarrier, so a thread
-// that gave up cannot leave the others blocked forever).
-__device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, bool& abort_flag) {
-  if (abort_flag) return false;
-  mbar_arrive(bar);
-  const bool ok = mbar_wait(bar, phase, kDetEpiSync, abort_flag);
-  phase ^= 1u;
-  return ok;
+// Upper levels of the slice tree: sum of n (1, 2, 4 or 8) aligned subtree sums.
+__device__ __forceinline__ float tree_sum(const float* v, int n) {
+  if (n == 1) return v[0];
+  if (n == 2) return __fadd_rn(v[0], v[1]);
+  if (n == 4) return __fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3]));
+  return __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])),
+                   __fadd_rn(__fadd_rn(v[4], v[5]), __fadd_rn(v[6], v[7])));
+}
+
+template <typename T>
+__device__ __forceinline__ void emit_chunk(const Params& p, T* C, int mode, int n, bool n_ok, int m_first,
+                                           const float (&t)[32]) {
+  if (!n_ok) return;
+  if (mode == FOLD) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int m = m_first + j;
+      if (m < p.M) C[static_cast<int64_t>(m) * p.ldc + n] = from_f32<T>(t[j]);
+    }
+  } else if (mode == ATOMIC) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int m = m_first + j;
+      if (m < p.M) atomicAdd(p.ws + static_cast<int64_t>(m) * p.N + n, t[j]);
+    }
+  } else {
+    // SPLIT (ws already offset to this unit's group) or PARTIAL
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int m = m_first + j;
+      if (m < p.M) p.ws[static_cast<int64_t>(m) * p.N + n] = t[j];
+    }
+  }
 }
 
 template <typename T, int FMT>
@@ -112,29 +167,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* ep_bar = acc_empty + 2;
-  uint64_t* drain_bar = ep_bar + 1;
+  const int n_stages = stages_for(p.a_rows);
+  const int stage_bytes = stage_bytes_for(p.a_rows);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingBytes);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* slot_full = empty + kMaxStages;
+  uint64_t* slot_free = slot_full + kSlots;
+  uint64_t* drain_bar = slot_free + kSlots;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
-  int* last_flag = reinterpret_cast<int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-#pragma unroll
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < n_stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(&acc_full[0], 1);
-    mbar_init(&acc_full[1], 1);
-    mbar_init(&acc_empty[0], kEpiThreads);
-    mbar_init(&acc_empty[1], kEpiThreads);
-    mbar_init(ep_bar, kEpiThreads);
+#pragma unroll
+    for (int k = 0; k < kSlots; ++k) {
+      mbar_init(&slot_full[k], 1);
+      mbar_init(&slot_free[k], kEpiThreads);
+    }
     mbar_init(drain_bar, 1);
     fence_mbar_init();
   }
@@ -150,6 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_wait();                 // inputs of this call may come from the previous kernel
+  if (threadIdx.x == 0) pdl_launch_dependents();
 
   const int n_groups = (p.slice_end - p.slice_begin) / p.group;
   const int units = p.n_tiles * p.m_tiles * n_groups;
@@ -161,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int fills = 0;                     // stage fills issued so far (round robin)
+      const uint32_t tx_bytes = kWTileBytes + p.a_rows * kBK * 2;
       for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x) {
         const int g = u % n_groups;
         const int t = u / n_groups;
@@ -173,14 +230,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int nkb = (k1 - k0 + kBK - 1) / kBK;
           for (int kb = 0; kb < nkb; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, kDetProdEmpty, abort_flag)) break;
-            uint8_t* st = smem + stage * kStageBytes;
-            mbar_arrive_expect_tx(&full[stage], kWTileBytes + p.a_rows * kBK * 2);
+            uint8_t* st = smem + stage * stage_bytes;
+            mbar_arrive_expect_tx(&full[stage], tx_bytes);
             const int kk = k0 + kb * kBK;
             tma_load_2d(st, &tmB, &full[stage], nt * kTileN, kk);
             tma_load_2d(st + kWBoxBytes, &tmB, &full[stage], nt * kTileN + 64, kk);
             tma_load_2d(st + kWTileBytes, &tmA, &full[stage], kk, mt * kTileM);
             ++fills;
-            if (++stage == kStages) {
+            if (++stage == n_stages) {
               stage = 0;
               phase ^= 1u;
             }
@@ -189,9 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain: every copy this thread issued must have landed before the CTA exits.
       bool drain_abort = false;
-#pragma unroll 1
-      for (int f = (fills > kStages ? fills - kStages : 0); f < fills; ++f) {
-        mbar_wait(&full[f % kStages], static_cast<uint32_t>((f / kStages) & 1), kDetDrain, drain_abort);
+      for (int f = (fills > n_stages ? fills - n_stages : 0); f < fills; ++f) {
+        mbar_wait(&full[f % n_stages], static_cast<uint32_t>((f / n_stages) & 1), kDetDrain, drain_abort);
       }
     }
   } else if (warp == 1) {
@@ -200,25 +256,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool abort_flag = false;
       int stage = 0;
       uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
+      uint32_t use_par = 0;   // bit k: parity of the number of times slot k has been written
+      int ordinal = 0;
       constexpr uint32_t idesc = umma_idesc_f16(FMT, /*a_mn=*/1, /*b_mn=*/0, kTileN, kTileM);
-      for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x) {
+      for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++ordinal) {
         const int g = u % n_groups;
         for (int si = 0; si < p.group && !abort_flag; ++si) {
           const int s = p.slice_begin + g * p.group + si;
           int k0, k1;
           slice_bounds(p, s, k0, k1);
           const int nkb = (k1 - k0 + kBK - 1) / kBK;
-          if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, kDetMmaAccEmpty, abort_flag)) break;
+          const int slot = slot_of(si, ordinal, p.group);
+          // the slot's previous value must have been released by the epilogue
+          if (!mbar_wait(&slot_free[slot], ((use_par >> slot) & 1u) ^ 1u, kDetMmaSlotFree, abort_flag)) break;
+          use_par ^= 1u << slot;
           tc_fence_after();
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTileM);
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * kTileM);
           for (int kb = 0; kb < nkb; ++kb) {
             if (!mbar_wait(&full[stage], phase, kDetMmaFull, abort_flag)) break;
             tc_fence_after();
             const int kk = k0 + kb * kBK;
             const int nsteps = min(kBK / kUK, (k1 - kk + kUK - 1) / kUK);
-            const uint32_t b_base = smem_u32(smem + stage * kStageBytes);
+            const uint32_t b_base = smem_u32(smem + stage * stage_bytes);
             const uint32_t a_base = b_base + kWTileBytes;
             for (int j = 0; j < nsteps; ++j) {
               // B (weights) MN-major, 128B swizzle: 64-column groups 8 KB apart (LBO),
@@ -229,15 +288,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               tc_mma_f16(d_tmem, bdesc, adesc, idesc, (kb > 0 || j > 0) ? 1u : 0u);
             }
             tc_commit(&empty[stage]);
-            if (++stage == kStages) {
+            if (++stage == n_stages) {
               stage = 0;
               phase ^= 1u;
             }
           }
           if (abort_flag) break;
-          tc_commit(&acc_full[acc]);
-          acc ^= 1;
-          if (acc == 0) acc_phase ^= 1u;
+          tc_commit(&slot_full[slot]);
         }
       }
       // Drain: all MMAs issued by this thread complete before TMEM is released.
@@ -249,19 +306,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue: 8 warps ----------------
     // Warp w may only read TMEM lanes 32*(w%4)..+31 (its quarter); the two warps
     // of a quarter split the 128 token columns into halves.  Thread <-> TMEM
-    // lane <-> output column n; each thread folds 64 token columns.
+    // lane <-> output column n; each thread handles 64 token columns.
     bool abort_flag = false;
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int n_local = quarter * 32 + lane;      // D row = weight column inside the tile
     const int col0 = half * kEpiCols;             // first token column of this thread
-    const int ep_tid = threadIdx.x - 64;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    uint32_t ep_phase = 0;
+    uint32_t use_par = 0;                         // bit k: parity of slot k's fills consumed
+    int ordinal = 0;
     T* C = reinterpret_cast<T*>(p.c);
     const int64_t MN = static_cast<int64_t>(p.M) * p.N;
-    for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x) {
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(col0);
+    for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++ordinal) {
       const int g = u % n_groups;
       const int t = u / n_groups;
       const int mt = t % p.m_tiles;
@@ -269,112 +325,79 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = nt * kTileN + n_local;
       const int m0 = mt * kTileM + col0;
       const bool n_ok = n < p.N;
-      const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      Params q = p;
+      if (p.mode == SPLIT) q.ws = p.ws + static_cast<int64_t>(g) * MN;
+      uint32_t stack = 0;                        // slot of the pending left operand of level l: bits 2l..2l+1
+
       for (int si = 0; si < p.group; ++si) {
         const int s = p.slice_begin + g * p.group + si;
         int k0, k1;
         slice_bounds(p, s, k0, k1);
         const bool empty_slice = (k1 <= k0);
-        if (!mbar_wait(&acc_full[acc], acc_phase, kDetEpiAccFull, abort_flag)) break;
+        const int slot = slot_of(si, ordinal, p.group);
+        if (!mbar_wait(&slot_full[slot], (use_par >> slot) & 1u, kDetEpiSlotFull, abort_flag)) break;
+        use_par ^= 1u << slot;
         tc_fence_after();
-        const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * kTileM + col0);
-        const uint32_t saddr = lane_base + static_cast<uint32_t>(kSumCol + col0);
+        const int nlev = __ffs(~si) - 1;          // trailing ones of si: tree levels closed here
+        const bool last = (si + 1 == p.group);
+        const uint32_t x_addr = lane_base + static_cast<uint32_t>(slot * kTileM);
+        if (nlev == 0 && !last) {
+          // a left operand: it waits in its slot (an empty slice is stored as zeros)
+          if (empty_slice) {
+            float z[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) z[j] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < kEpiCols / 32; ++c) tmem_st_32x32b_x32(x_addr + c * 32, z);
+            tmem_st_wait();
+          }
+          stack = (stack & ~3u) | static_cast<uint32_t>(slot);
+          continue;
+        }
+        const int res_slot = (nlev > 0) ? static_cast<int>((stack >> (2 * (nlev - 1))) & 3u) : slot;
 #pragma unroll 1
         for (int c = 0; c < kEpiCols / 32; ++c) {
-          float v[32];
-          tmem_ld_32x32b_x32(taddr + c * 32, v);
-          tmem_ld_wait();
+          float acc[32];
           if (empty_slice) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+            for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
+          } else {
+            tmem_ld_32x32b_x32(x_addr + c * 32, acc);
+            tmem_ld_wait();
           }
-          if (p.mode == FOLD) {
-            // running fold ((p0 + p1) + p2) + ... kept in TMEM columns [kSumCol, kSumCol + 128)
-            if (si > 0) {
-              float w[32];
-              tmem_ld_32x32b_x32(saddr + c * 32, w);
-              tmem_ld_wait();
+          // close the tree levels: acc = stack[l] + acc for l = 0 .. nlev-1
+#pragma unroll 1
+          for (int l = 0; l < nlev; ++l) {
+            float left[32];
+            const uint32_t ls = (stack >> (2 * l)) & 3u;
+            tmem_ld_32x32b_x32(lane_base + ls * kTileM + c * 32, left);
+            tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(w[j], v[j]);
-            }
-            if (si + 1 < p.group) {
-              tmem_st_32x32b_x32(saddr + c * 32, v);
-              tmem_st_wait();
-            } else if (n_ok) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int m = m0 + c * 32 + j;
-                if (m < p.M) C[static_cast<int64_t>(m) * p.ldc + n] = from_f32<T>(v[j]);
-              }
-            }
-          } else if (p.mode == ATOMIC) {
-            if (n_ok) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int m = m0 + c * 32 + j;
-                if (m < p.M) atomicAdd(p.ws + static_cast<int64_t>(m) * p.N + n, v[j]);
-              }
-            }
-          } else {  // SPLIT / PARTIAL: partial of slice s -> ws[s - slice_begin][m][n]
-            if (n_ok) {
-              float* dst = p.ws + static_cast<int64_t>(s - p.slice_begin) * MN;
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int m = m0 + c * 32 + j;
-                if (m < p.M) dst[static_cast<int64_t>(m) * p.N + n] = v[j];
-              }
-            }
+            for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(left[j], acc[j]);
+          }
+          if (last) {
+            emit_chunk<T>(q, C, p.mode, n, n_ok, m0 + c * 32, acc);
+          } else {
+            tmem_st_32x32b_x32(lane_base + static_cast<uint32_t>(res_slot * kTileM) + c * 32, acc);
           }
         }
+        if (!last) tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&acc_empty[acc]);
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
+        // release every slot consumed here; the result slot stays unless this was the unit's end
+        if (nlev > 0) mbar_arrive(&slot_free[slot]);
+        for (int l = 0; l + 1 < nlev; ++l) mbar_arrive(&slot_free[(stack >> (2 * l)) & 3u]);
+        if (last) mbar_arrive(&slot_free[res_slot]);
+        if (!last) stack = (stack & ~(3u << (2 * nlev))) | (static_cast<uint32_t>(res_slot) << (2 * nlev));
       }
       if (abort_flag) break;
 
-      if (p.mode == SPLIT) {
-        // Last CTA to finish this tile folds all slices in slice order.
-        __threadfence();
-        if (!epi_sync(ep_bar, ep_phase, abort_flag)) break;
-        if (ep_tid == 0) {
-          const int tile = nt * p.m_tiles + mt;
-          const int arrivals = (p.slice_end - p.slice_begin) / p.group;
-          const int old = atomicAdd(p.counters + tile, 1);
-          *last_flag = (old == arrivals - 1) ? 1 : 0;
-          if (old == arrivals - 1) p.counters[tile] = 0;  // ready for the next launch
-        }
-        if (!epi_sync(ep_bar, ep_phase, abort_flag)) break;
-        const bool is_last = *last_flag != 0;
-        if (is_last && n_ok) {
-          __threadfence();
-          const int rows = min(kEpiCols, p.M - m0);
-          // 4 rows x 8 slices of independent loads in flight per iteration
-          for (int i0 = 0; i0 < rows; i0 += 4) {
-            float part[4][kSlices];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-              const float* src = p.ws + static_cast<int64_t>(m0 + min(i0 + r, rows - 1)) * p.N + n;
-#pragma unroll
-              for (int s = 0; s < kSlices; ++s) part[r][s] = __ldcg(src + s * MN);
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-              if (i0 + r < rows) {
-                float a = part[r][0];
-#pragma unroll
-                for (int s = 1; s < kSlices; ++s) a = __fadd_rn(a, part[r][s]);
-                C[static_cast<int64_t>(m0 + i0 + r) * p.ldc + n] = from_f32<T>(a);
-              }
-            }
-          }
-        }
-        // keep last_flag stable until every thread has read it
-        if (!epi_sync(ep_bar, ep_phase, abort_flag)) break;
-      }
     }
   }
 
+  // Each warp converges before the CTA barrier: in warps 0 and 1 only lane 0
+  // ran the producer / MMA loop, and an aligned barrier must be reached by the
+  // whole warp together, or it can release before the epilogue is done.
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -383,17 +406,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// out[m, n] = fold of 8 slice partials in slice order (row-parallel TP combine).
+// out[m, n] = upper tree levels over n_parts aligned subtree sums, partials
+// [n_parts][M][N] f32.  Used by SPLIT launches (as a programmatic dependent of
+// the GEMM) and for the row-parallel TP combine.  Each thread sums 4
+// consecutive columns with 16-byte loads when N allows.
 template <typename T>
-__global__ void fold_slices_kernel(const float* __restrict__ partials, T* __restrict__ c, int64_t ldc, int M, int N) {
+__global__ void __launch_bounds__(256) fold_groups_kernel(const float* __restrict__ partials, int n_parts,
+                                                          T* __restrict__ c, int64_t ldc, int M, int N) {
+  pdl_wait();
   const int64_t MN = static_cast<int64_t>(M) * N;
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < MN;
+  const int64_t quads = (static_cast<int64_t>(N) + 3) / 4;
+  const int64_t total = static_cast<int64_t>(M) * quads;
+  const bool vec = (N % 4) == 0;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t m = idx / N, n = idx - m * N;
-    float a = partials[idx];
+    const int64_t m = idx / quads;
+    const int n0 = static_cast<int>(idx - m * quads) * 4;
+    const int64_t base = m * N + n0;
+    float v[kSlices][4];
 #pragma unroll
-    for (int s = 1; s < kSlices; ++s) a = __fadd_rn(a, partials[idx + s * MN]);
-    c[m * ldc + n] = from_f32<T>(a);
+    for (int j = 0; j < kSlices; ++j) {
+      if (j < n_parts) {
+        if (vec) {
+          const float4 q = __ldcg(reinterpret_cast<const float4*>(partials + j * MN + base));
+          v[j][0] = q.x;
+          v[j][1] = q.y;
+          v[j][2] = q.z;
+          v[j][3] = q.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[j][e] = (n0 + e < N) ? __ldcg(partials + j * MN + base + e) : 0.0f;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[j][e] = 0.0f;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (n0 + e < N) {
+        float col[kSlices];
+#pragma unroll
+        for (int j = 0; j < kSlices; ++j) col[j] = v[j][e];
+        c[m * ldc + n0 + e] = from_f32<T>(tree_sum(col, n_parts));
+      }
+    }
   }
 }
 

@@ -9,6 +9,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "dk_common.cuh"
 #include "dk_rmsnorm.cuh"
@@ -37,6 +38,26 @@ int check_launch(const char* what) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launch with programmatic stream serialization: the kernel may begin (and run
+// its preamble) while the previous kernel on the stream finishes; every kernel
+// of this library waits for its predecessor (griddepcontrol.wait) before it
+// touches global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 constexpr int kMaxDevices = 64;
 
@@ -197,6 +218,11 @@ struct GemmPlan {
 // plus the L2 round trip of the f32 slice partials when slices are spread
 // over CTAs -- picks the cheapest of 8 (FOLD), 4, 2, 1 (SPLIT).
 int pick_group(int64_t M, int64_t N, int64_t K, int64_t tiles, int sms) {
+#ifdef DK_GEMM_FORCE_GROUP
+  (void)M; (void)N; (void)K; (void)tiles; (void)sms;
+  return DK_GEMM_FORCE_GROUP;
+#endif
+  const int a_rows = (M <= dk::gemm::kTileM) ? static_cast<int>(ceil_div(M, 8) * 8) : dk::gemm::kTileM;
   const double kSmBytesPerUs = 100e3;   // sustained TMA bytes per SM per microsecond
   const double kL2BytesPerUs = 10e6;    // L2 bytes per microsecond for the partial round trip
   const int64_t kb_per_slice = ceil_div(slice_len_for(K, dk::gemm::kSlices), dk::gemm::kBK);
@@ -205,8 +231,9 @@ int pick_group(int64_t M, int64_t N, int64_t K, int64_t tiles, int sms) {
   for (int g = dk::gemm::kSlices; g >= 1; g /= 2) {
     const int64_t units = tiles * (dk::gemm::kSlices / g);
     const int64_t waves = ceil_div(units, sms);
-    const double load = static_cast<double>(waves) * g * kb_per_slice * dk::gemm::kStageBytes / kSmBytesPerUs;
-    const double part = (g < dk::gemm::kSlices) ? 2.0 * dk::gemm::kSlices * M * N * 4 / kL2BytesPerUs : 0.0;
+    const double load = static_cast<double>(waves) * g * kb_per_slice * dk::gemm::stage_bytes_for(a_rows) / kSmBytesPerUs;
+    // each unit writes one subtree sum; the last arriver reads them back
+    const double part = (g < dk::gemm::kSlices) ? 2.0 * (dk::gemm::kSlices / g) * M * N * 4 / kL2BytesPerUs : 0.0;
     const double t = load + part;
     if (t < best * 0.97) {
       best = t;
@@ -227,7 +254,7 @@ GemmPlan plan_invariant(int64_t M, int64_t N, int64_t K, int sms) {
   if (pl.mode == dk::gemm::SPLIT) {
     pl.counters_off = 0;
     pl.partials_off = kCounterBytes;
-    pl.ws_bytes = pl.partials_off + sizeof(float) * static_cast<size_t>(dk::gemm::kSlices) * M * N;
+    pl.ws_bytes = pl.partials_off + sizeof(float) * static_cast<size_t>(dk::gemm::kSlices / group) * M * N;
   }
   return pl;
 }
@@ -244,6 +271,17 @@ int gemm_validate(const void* a, int64_t lda, const void* b, int64_t ldb, int64_
   if (lda % 8 != 0 || ldb % 8 != 0)
     return fail(DK_ERR_INVALID_ARGUMENT, "%s: lda and ldb must be multiples of 8 elements", what);
   if (lda < K || ldb < N) return fail(DK_ERR_INVALID_ARGUMENT, "%s: leading dimension too small", what);
+  return DK_OK;
+}
+
+template <typename T>
+int launch_fold(const float* partials, int n_parts, void* c, int64_t ldc, int M, int N, cudaStream_t st) {
+  const int64_t total = static_cast<int64_t>(M) * ceil_div(N, 4);
+  const int64_t want = ceil_div(total, 256);
+  const int blocks = static_cast<int>(want < 8 * 148 ? want : 8 * 148);
+  cudaError_t e = launch_pdl(dk::gemm::fold_groups_kernel<T>, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, st,
+                             partials, n_parts, static_cast<T*>(c), ldc, M, N);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "matmul fold: launch failed: %s", cudaGetErrorString(e));
   return DK_OK;
 }
 
@@ -268,16 +306,24 @@ int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ld
   const int sms = sm_count(current_device());
   const int grid = static_cast<int>(units < sms ? units : sms);
   if (grid <= 0) return DK_OK;
+  cudaError_t e;
   if (dtype == DK_BF16) {
     static bool done[kMaxDevices] = {false};
     auto fn = dk::gemm::gemm_kernel<__nv_bfloat16, 1>;
     if ((rc = ensure_smem(fn, dk::gemm::kSmemBytes, done))) return rc;
-    fn<<<grid, dk::gemm::kThreads, dk::gemm::kSmemBytes, st>>>(tmB, tmA, p);
+    e = launch_pdl(fn, dim3(grid), dim3(dk::gemm::kThreads), dk::gemm::kSmemBytes, st, tmB, tmA, p);
   } else {
     static bool done[kMaxDevices] = {false};
     auto fn = dk::gemm::gemm_kernel<__half, 0>;
     if ((rc = ensure_smem(fn, dk::gemm::kSmemBytes, done))) return rc;
-    fn<<<grid, dk::gemm::kThreads, dk::gemm::kSmemBytes, st>>>(tmB, tmA, p);
+    e = launch_pdl(fn, dim3(grid), dim3(dk::gemm::kThreads), dk::gemm::kSmemBytes, st, tmB, tmA, p);
+  }
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  if (p.mode == dk::gemm::SPLIT) {
+    // the upper tree levels over the groups' subtree sums, as a dependent launch
+    const int n_parts = (p.slice_end - p.slice_begin) / p.group;
+    if (dtype == DK_BF16) return launch_fold<__nv_bfloat16>(p.ws, n_parts, p.c, p.ldc, p.M, p.N, st);
+    return launch_fold<__half>(p.ws, n_parts, p.c, p.ldc, p.M, p.N, st);
   }
   return check_launch(what);
 }
@@ -287,14 +333,6 @@ int zero_output(void* c, int64_t ldc, int64_t M, int64_t N, int elem, cudaStream
   cudaError_t e = cudaMemset2DAsync(c, ldc * elem, 0, N * elem, M, st);
   if (e != cudaSuccess) return fail(DK_ERR_CUDA, "matmul: memset: %s", cudaGetErrorString(e));
   return DK_OK;
-}
-
-template <typename T>
-int launch_fold(const float* partials, void* c, int64_t ldc, int M, int N, cudaStream_t st) {
-  const int64_t MN = static_cast<int64_t>(M) * N;
-  const int blocks = static_cast<int>(ceil_div(MN, 256) < 4096 ? ceil_div(MN, 256) : 4096);
-  dk::gemm::fold_slices_kernel<T><<<blocks, 256, 0, st>>>(partials, static_cast<T*>(c), ldc, M, N);
-  return check_launch("matmul_fold_slices");
 }
 
 template <typename T>
@@ -495,13 +533,10 @@ int dk_matmul_batch_invariant(const void* a, int64_t lda, const void* b, int64_t
   p.c = c;
   p.ldc = ldc;
   if (pl.mode == dk::gemm::SPLIT) {
-    if (static_cast<int64_t>(pl.n_tiles) * pl.m_tiles > kMaxCounters)
-      return fail(DK_ERR_INVALID_ARGUMENT, "%s: too many output tiles for the counter area", what);
     if (!workspace || workspace_bytes < pl.ws_bytes)
       return fail(DK_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", what, pl.ws_bytes,
                   workspace_bytes);
     if (!aligned16(workspace)) return fail(DK_ERR_WORKSPACE, "%s: workspace must be 16-byte aligned", what);
-    p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + pl.counters_off);
     p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.partials_off);
   }
   return gemm_launch(dtype, a, lda, b, ldb, p, st, what);
@@ -512,13 +547,17 @@ int dk_matmul_slice_partials(const void* a, int64_t lda, const void* b, int64_t 
   const char* what = "matmul_slice_partials";
   int rc = gemm_validate(a, lda, b, ldb, M, N, K, dtype, what);
   if (rc) return rc;
-  if (slice_begin < 0 || slice_end > dk::gemm::kSlices || slice_begin >= slice_end)
-    return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad slice range [%d, %d)", what, slice_begin, slice_end);
+  const int span = slice_end - slice_begin;
+  if (slice_begin < 0 || slice_end > dk::gemm::kSlices || span <= 0 || (span & (span - 1)) != 0 ||
+      slice_begin % span != 0)
+    return fail(DK_ERR_INVALID_ARGUMENT,
+                "%s: slice range [%d, %d) is not an aligned group of 1, 2, 4 or 8 slices", what, slice_begin,
+                slice_end);
   if (M == 0 || N == 0) return DK_OK;
   if (!partials) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null partials", what);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (K == 0) {
-    cudaError_t e = cudaMemsetAsync(partials, 0, sizeof(float) * (slice_end - slice_begin) * M * N, st);
+    cudaError_t e = cudaMemsetAsync(partials, 0, sizeof(float) * M * N, st);
     return e == cudaSuccess ? DK_OK : fail(DK_ERR_CUDA, "%s: memset: %s", what, cudaGetErrorString(e));
   }
   dk::gemm::Params p{};
@@ -528,7 +567,7 @@ int dk_matmul_slice_partials(const void* a, int64_t lda, const void* b, int64_t 
   p.slice_len = slice_len_for(K, dk::gemm::kSlices);
   p.slice_begin = slice_begin;
   p.slice_end = slice_end;
-  p.group = 1;
+  p.group = span;
   p.n_tiles = static_cast<int>(ceil_div(N, dk::gemm::kTileN));
   p.m_tiles = static_cast<int>(ceil_div(M, dk::gemm::kTileM));
   p.mode = dk::gemm::PARTIAL;
@@ -536,16 +575,18 @@ int dk_matmul_slice_partials(const void* a, int64_t lda, const void* b, int64_t 
   return gemm_launch(dtype, a, lda, b, ldb, p, st, what);
 }
 
-int dk_matmul_fold_slices(const float* partials, void* c, int64_t ldc, int64_t M, int64_t N, int dtype,
+int dk_matmul_fold_slices(const float* partials, int n_parts, void* c, int64_t ldc, int64_t M, int64_t N, int dtype,
                           void* stream) {
   if (dtype != DK_BF16 && dtype != DK_F16) return fail(DK_ERR_UNSUPPORTED, "matmul_fold_slices: bad dtype");
+  if (n_parts != 1 && n_parts != 2 && n_parts != 4 && n_parts != 8)
+    return fail(DK_ERR_INVALID_ARGUMENT, "matmul_fold_slices: n_parts must be 1, 2, 4 or 8");
   if (M < 0 || N < 0 || M > 0x7fffffffLL || N > 0x7fffffffLL)
     return fail(DK_ERR_INVALID_ARGUMENT, "matmul_fold_slices: bad shape");
   if (M == 0 || N == 0) return DK_OK;
   if (!partials || !c || ldc < N) return fail(DK_ERR_INVALID_ARGUMENT, "matmul_fold_slices: bad pointer/ldc");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == DK_BF16) return launch_fold<__nv_bfloat16>(partials, c, ldc, (int)M, (int)N, st);
-  return launch_fold<__half>(partials, c, ldc, (int)M, (int)N, st);
+  if (dtype == DK_BF16) return launch_fold<__nv_bfloat16>(partials, n_parts, c, ldc, (int)M, (int)N, st);
+  return launch_fold<__half>(partials, n_parts, c, ldc, (int)M, (int)N, st);
 }
 
 int dk_matmul_batch_variant(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc, int64_t M,

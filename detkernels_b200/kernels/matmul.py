@@ -5,15 +5,16 @@ Drop-in for the reference's ``kernels/matmul.py``:
 * ``matmul_reference`` (matmul.py:42-49): f32 ``a @ b`` cast back to a's dtype.
 * ``matmul_batch_invariant`` (matmul.py:161-186): tcgen05/TMEM GEMM fed by
   TMA with one tile shape for every M and K reduced as 8 fixed slices folded
-  in slice order -- a row's bits never depend on M.  ``block_m/n/k`` are
+  along a fixed tree -- a row's bits never depend on M.  ``block_m/n/k`` are
   accepted for signature compatibility; the tile shape is fixed.
 * ``matmul_batch_variant`` (matmul.py:189-228): split-K with f32 atomics when
   ``M < split_m_threshold``.
 
-Extensions used by tensor parallelism: ``matmul_slice_partials`` (f32
-partials of a contiguous range of the 8 K slices) and ``matmul_fold_slices``
-(sum of all 8 partials in slice order), which together reproduce
-``matmul_batch_invariant`` bit for bit.
+The 8 K-slice partials are summed along the fixed tree
+((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)).  Extensions used by tensor parallelism:
+``matmul_slice_partials`` (f32 subtree sum of one aligned group of slices) and
+``matmul_fold_slices`` (the upper tree levels over the groups' sums), which
+together reproduce ``matmul_batch_invariant`` bit for bit.
 
 A and B must be bf16 or f16 (same dtype); the output has a's dtype.
 """
@@ -108,14 +109,14 @@ def matmul_batch_variant(a, b, split_m_threshold: int = 64, split_k: int = 4,
 
 
 def matmul_slice_partials(a, b, slice_begin: int, slice_end: int, out=None):
-    """f32 partials of K slices [slice_begin, slice_end): shape [slice_end - slice_begin, M, N]."""
+    """f32 [M, N] subtree sum of the aligned slice group [slice_begin, slice_end)
+    (1, 2, 4 or 8 of the 8 K slices; slice_begin a multiple of the group size)."""
     import torch
 
     M, K, N = _check_inputs(a, b, "matmul_slice_partials")
-    n = slice_end - slice_begin
     if out is None:
-        out = torch.empty((n, M, N), device=a.device, dtype=torch.float32)
-    assert out.shape == (n, M, N) and out.dtype == torch.float32 and out.is_contiguous()
+        out = torch.empty((M, N), device=a.device, dtype=torch.float32)
+    assert out.shape == (M, N) and out.dtype == torch.float32 and out.is_contiguous()
     if M == 0 or N == 0:
         return out
     a2, b2 = _tma_ready(a), _tma_ready(b)
@@ -123,21 +124,23 @@ def matmul_slice_partials(a, b, slice_begin: int, slice_end: int, out=None):
         a2.data_ptr(), a2.stride(0), b2.data_ptr(), b2.stride(0), out.data_ptr(), M, N, K, int(slice_begin),
         int(slice_end), _lib.dtype_code(a.dtype), _lib.stream_ptr(a.device))
     _lib.check(rc, "matmul_slice_partials")
+    _lib.count_launch()
     return out
 
 
 def matmul_fold_slices(partials, dtype, out=None):
-    """Fold [8, M, N] f32 partials in slice order and round to ``dtype``."""
+    """Sum [n, M, N] f32 subtree sums of n equal aligned slice groups (n in 1, 2, 4, 8, in
+    group order) along the upper levels of the slice tree and round to ``dtype``."""
     import torch
 
     assert partials.is_cuda and partials.dtype == torch.float32 and partials.is_contiguous()
-    assert partials.shape[0] == K_SLICES, "need all %d slices" % K_SLICES
-    _, M, N = partials.shape
+    n_parts, M, N = partials.shape
     if out is None:
         out = torch.empty((M, N), device=partials.device, dtype=dtype)
     if M == 0 or N == 0:
         return out
-    rc = _lib.load().dk_matmul_fold_slices(partials.data_ptr(), out.data_ptr(), out.stride(0), M, N,
+    rc = _lib.load().dk_matmul_fold_slices(partials.data_ptr(), int(n_parts), out.data_ptr(), out.stride(0), M, N,
                                            _lib.dtype_code(dtype), _lib.stream_ptr(partials.device))
     _lib.check(rc, "matmul_fold_slices")
+    _lib.count_launch()
     return out

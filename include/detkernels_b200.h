@@ -52,7 +52,7 @@ extern "C" {
 #define DK_BF16 2
 
 /* ---- fixed numerics of the invariant kernels (part of the output definition) ---- */
-#define DK_MATMUL_K_SLICES 8        /* K is reduced as 8 fixed slices, folded ((p0+p1)+p2)+... in f32 */
+#define DK_MATMUL_K_SLICES 8        /* K is reduced as 8 fixed slices, summed along a fixed f32 tree */
 #define DK_ATTN_KV_SPLIT 256        /* decode attention reduces KV in fixed splits of 256 tokens */
 #define DK_RMSNORM_THREADS 256      /* one CTA of 256 threads per row */
 
@@ -94,7 +94,8 @@ int dk_rmsnorm_batch_variant(const void* x, int64_t x_row_stride, const void* we
  * in elements; lda and ldb must be multiples of 8 and A, B 16-byte aligned
  * (TMA).  The invariant kernel reduces K as DK_MATMUL_K_SLICES fixed slices of
  * ceil16(K/8) elements, each accumulated by tcgen05 in ascending 16-wide K
- * steps into its own f32 TMEM accumulator, then folded in slice order. */
+ * steps into its own f32 TMEM accumulator (partial p_s), then summed along the
+ * fixed tree ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)) and rounded to the dtype. */
 
 /* Scratch bytes the invariant / variant matmul may need for this shape. */
 size_t dk_matmul_workspace_size(int64_t M, int64_t N, int64_t K);
@@ -102,15 +103,16 @@ size_t dk_matmul_workspace_size(int64_t M, int64_t N, int64_t K);
 int dk_matmul_batch_invariant(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
                               int64_t M, int64_t N, int64_t K, int dtype, void* workspace,
                               size_t workspace_bytes, void* stream);
-/* Same numerics, but only slices [slice_begin, slice_end) are computed and each slice's f32
- * partial is written to partials[(s - slice_begin) * M * N + m * N + n] (row-parallel tensor
- * parallelism: every rank computes its own slices; dk_matmul_fold_slices sums them in order). */
-int dk_matmul_slice_partials(const void* a, int64_t lda, const void* b, int64_t ldb, float* partials,
+/* Same numerics for one aligned group of slices [slice_begin, slice_end) (1, 2, 4 or 8 slices,
+ * slice_begin a multiple of the group size): writes that group's subtree sum to partial[m * N + n]
+ * (f32).  Row-parallel tensor parallelism: rank r of a TP-way split computes group r. */
+int dk_matmul_slice_partials(const void* a, int64_t lda, const void* b, int64_t ldb, float* partial,
                              int64_t M, int64_t N, int64_t K, int slice_begin, int slice_end, int dtype,
                              void* stream);
-/* out[m,n] = round(((p0 + p1) + p2) + ... + p7) with p_s = partials[s*M*N + m*N + n]. */
-int dk_matmul_fold_slices(const float* partials, void* c, int64_t ldc, int64_t M, int64_t N, int dtype,
-                          void* stream);
+/* out[m,n] = the upper tree levels over n_parts (1, 2, 4 or 8) subtree sums in group order,
+ * partials[j * M * N + m * N + n], rounded to dtype: reproduces dk_matmul_batch_invariant bit for bit. */
+int dk_matmul_fold_slices(const float* partials, int n_parts, void* c, int64_t ldc, int64_t M, int64_t N,
+                          int dtype, void* stream);
 /* Scratch bytes dk_matmul_batch_variant needs on its split-K path. */
 size_t dk_matmul_variant_workspace_size(int64_t M, int64_t N);
 /* replaces kernels/matmul.py:189-228 matmul_batch_variant: when M < split_m_threshold, K is split

@@ -104,21 +104,24 @@ def test_baseline_config_row0_bitwise_across_M(dev, N):
 
 
 def test_slice_partials_fold_reproduce_invariant_output(dev):
-    """TP decomposition: partials of slices [0,2),[2,4),[4,8) folded in slice order
-    equal the single-call result bit for bit (any split of the slices)."""
+    """TP decomposition: for every TP degree (1, 2, 4, 8 aligned slice groups) the
+    groups' subtree sums folded along the upper tree equal the single call bit for bit."""
     import torch
     from detkernels_b200.kernels.matmul import (matmul_batch_invariant, matmul_fold_slices,
                                                 matmul_slice_partials)
-    for (m, k, n) in [(5, 4096, 1024), (300, 2816, 1024), (1, 1024, 2816)]:
+    for (m, k, n) in [(5, 4096, 1024), (300, 2816, 1024), (1, 1024, 2816), (2048, 1024, 256)]:
         a, b = _random_input(dev, m, k, n, torch.bfloat16, seed=7, wscale=0.02)
         ref = matmul_batch_invariant(a, b)
-        parts = torch.cat([matmul_slice_partials(a, b, 0, 2), matmul_slice_partials(a, b, 2, 4),
-                           matmul_slice_partials(a, b, 4, 8)])
-        assert torch.equal(matmul_fold_slices(parts, torch.bfloat16), ref)
-        # partial sum of slice s alone is the product over that K range (f32 tolerance)
+        for tp in (1, 2, 4, 8):
+            g = 8 // tp
+            parts = torch.stack([matmul_slice_partials(a, b, r * g, (r + 1) * g) for r in range(tp)])
+            assert torch.equal(matmul_fold_slices(parts, torch.bfloat16), ref), (m, k, n, tp)
+        # a single slice's sum is the product over that K range (f32 tolerance)
         L = ((k + 7) // 8 + 15) // 16 * 16
         p3 = a[:, 3 * L:4 * L].float() @ b[3 * L:4 * L].float()
-        torch.testing.assert_close(parts[3], p3, rtol=1e-4, atol=1e-4)
+        torch.testing.assert_close(matmul_slice_partials(a, b, 3, 4), p3, rtol=1e-4, atol=1e-4)
+    with pytest.raises(ValueError):
+        matmul_slice_partials(a, b, 1, 3)   # not an aligned group
 
 
 def test_strided_and_unaligned_operands(dev):
