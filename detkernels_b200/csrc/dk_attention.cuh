@@ -16,16 +16,22 @@
 //     Scores come from mma.m16n8k16 (bf16/f16 in, f32 accumulate) with the q
 //     vector as one of the 16 MMA rows; probabilities are rounded to the input
 //     type for the P.V product and the same rounded values are summed into l.
-//   * The four warp states are merged in warp order 0..3, the split states in
-//     split order, each with weights exp2(m_i - max_i m_i); out = O / l.
+//   * The four warp states of a split are merged in warp order 0..3 with
+//     weights exp2(m_w - max_w m_w) into the split's (m, l, O).
+//   * The split states are merged in split order by a running (online) merge:
+//     m' = max(m, m_s); (l, O) <- (l, O) * exp2(m - m') + (l_s, O_s) * exp2(m_s - m');
+//     out = O / l.
 // A row's arithmetic therefore depends on its q, its KV sequence and its
 // kv_len only -- not on the batch, the other rows of its tile, or the grid.
 //
-// Work decomposition: one CTA per (row tile, kv head, split).  A producer warp
-// streams 64-token K/V blocks with TMA (4-D tensor map over the cache, 128- or
-// 64-byte swizzle) into a ring of shared-memory stages; four consumer warps
-// compute.  Multi-split tiles write (m, l, O) partials to the workspace and the
-// last CTA to arrive (atomic counter, no spinning) combines them.
+// Work decomposition: one CTA per (row tile, kv head, run of up to `spu`
+// consecutive splits).  A producer warp streams 64-token K/V blocks with TMA
+// (4-D tensor map over the cache, 128- or 64-byte swizzle) into a ring of
+// shared-memory stages that keeps flowing across split boundaries; four
+// consumer warps compute.  When one CTA covers all of a tile's splits it merges
+// them as it goes and writes the output; otherwise each CTA writes its splits'
+// (m, l, O) to the workspace and the last CTA to arrive (atomic counter, no
+// spinning) replays the same split-order merge over them.
 #pragma once
 
 #include "dk_common.cuh"
@@ -51,9 +57,12 @@ struct Cfg {
   static constexpr int STAGE_BYTES = 2 * TENSOR_BYTES;   // K block + V block
   static constexpr int STAGES = (D == 128) ? 3 : 4;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int COMB_BYTES = kConsumerWarps * kRows * (D + 2) * 4;
-  static_assert(COMB_BYTES <= RING_BYTES, "combine scratch reuses the ring");
-  static constexpr int SMEM_BYTES = RING_BYTES + 1024 + 512;
+  static constexpr int CSTRIDE = D + 8;                  // padded row of the warp-merge buffer (floats)
+  static constexpr int KMAX = (kRows * D + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32);
+  // dynamic shared memory for a launch whose tiles hold up to `rows` mma rows
+  static __host__ __device__ int smem_bytes(int rows) {
+    return 1024 + RING_BYTES + kConsumerWarps * rows * (CSTRIDE + 2) * 4 + 512;
+  }
 };
 
 struct Params {
@@ -65,9 +74,11 @@ struct Params {
   int32_t uniform_len;
   const int32_t* tiles;
   int32_t n_tiles;
-  int32_t rows_cap;   // workspace rows per (tile, kv head, split) = rows_per_tile * G
+  int32_t rows_cap;   // mma rows per tile (workspace rows and merge-buffer rows) = rows_per_tile * G
   int32_t n_rows, hq, hkv, G;
   int32_t max_splits;
+  int32_t spu;        // splits per CTA
+  int32_t upt;        // CTAs per (tile, kv head) = ceil(max_splits / spu)
   int32_t kv_capacity;
   int32_t kv_n_seq;
   float scale_log2;   // softmax scale * log2(e)
@@ -159,13 +170,36 @@ __device__ __forceinline__ float weight_of(float m, float mref) {
   return exp2f(__fsub_rn(m, mref));
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 2)
+// One step of the split-order merge: (m, l, o) <- merge((m, l, o), (ms, ls, os)).
+// `first` starts the merge with split 0's state.
+__device__ __forceinline__ void merge_split(bool first, float& m, float& l, float& o, float ms, float ls, float os) {
+  if (first) {
+    m = ms;
+    l = ls;
+    o = os;
+    return;
+  }
+  const float mn = fmaxf(m, ms);
+  const float mref = (mn == -INFINITY) ? 0.0f : mn;
+  const float a = weight_of(m, mref), b = weight_of(ms, mref);
+  l = __fadd_rn(__fmul_rn(l, a), __fmul_rn(ls, b));
+  o = __fadd_rn(__fmul_rn(o, a), __fmul_rn(os, b));
+  m = mn;
+}
+
+// KM: merge elements per consumer thread (ceil(rows x D / 128)); decode launches
+// without row tiles have at most G rows and use a narrow instance.
+template <typename T, int D, int KM>
+__global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
     attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const Params p) {
   using C = Cfg<D>;
+  static_assert(KM <= C::KMAX, "merge elements per thread");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + C::RING_BYTES);
+  float* comb_o = reinterpret_cast<float*>(ring + C::RING_BYTES);               // [4][rows_cap][CSTRIDE]
+  float* comb_ml = comb_o + kConsumerWarps * p.rows_cap * C::CSTRIDE;          // [4][rows_cap][2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(comb_ml + kConsumerWarps * p.rows_cap * 2) + 7) & ~uintptr_t(7));
   uint64_t* empty = full + C::STAGES;
   uint64_t* cbar = empty + C::STAGES;
   int* s_len = reinterpret_cast<int*>(cbar + 1);   // kv_len of each tile row [16]
@@ -173,10 +207,24 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  const int tile = blockIdx.x / p.max_splits;
-  const int split = blockIdx.x % p.max_splits;
+  const int tile = blockIdx.x / p.upt;
+  const int unit = blockIdx.x % p.upt;
   const int kvh = blockIdx.y;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    mbar_init(cbar, kConsumerWarps * 32);
+    fence_mbar_init();
+  }
+  if (warp == kConsumerWarps && lane == 0) {
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  pdl_wait();   // lengths, tiles and q may come from the previous kernel
+  if (threadIdx.x == 0) pdl_launch_dependents();
 
   // ---- tile description (identical in every CTA of the tile) ----
   int r0, nr, seq;
@@ -192,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int rows_per_tile_max = kRows / p.G;
   if (nr < 1 || nr > rows_per_tile_max || r0 < 0 || r0 + nr > p.n_rows || seq < 0 || seq >= p.kv_n_seq ||
       nr * p.G > p.rows_cap) {
-    if (threadIdx.x == 0 && split == 0 && kvh == 0) report_error(DK_ERR_DEVICE_CHECK, kDetTile);
+    if (threadIdx.x == 0 && unit == 0 && kvh == 0) report_error(DK_ERR_DEVICE_CHECK, kDetTile);
     return;
   }
   int max_len = 0;
@@ -203,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     max_len = max(max_len, L);
   }
   if (len_bad) {
-    if (threadIdx.x == 0 && split == 0 && kvh == 0) report_error(DK_ERR_DEVICE_CHECK, kDetLen);
+    if (threadIdx.x == 0 && unit == 0 && kvh == 0) report_error(DK_ERR_DEVICE_CHECK, kDetLen);
     return;
   }
   const int nsplits = (max_len + kSplit - 1) / kSplit;
@@ -212,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (nsplits == 0) {
     // every row of the tile has an empty KV sequence: output zeros
-    if (split == 0) {
+    if (unit == 0) {
       for (int e = threadIdx.x; e < valid_rows * D; e += blockDim.x) {
         const int rho = e / D, d = e % D;
         const int i = rho / p.G, gh = rho % p.G;
@@ -221,20 +269,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     return;
   }
-  if (split >= nsplits) return;
+  const int s_begin = unit * p.spu;
+  if (s_begin >= nsplits) return;
+  const int s_end = min(s_begin + p.spu, nsplits);
+  const bool direct = (nsplits <= p.spu);        // this CTA owns every split of the tile
 
-  const int tok_begin = split * kSplit;
-  const int tok_end = min(tok_begin + kSplit, max_len);
-  const int nblk = (tok_end - tok_begin + kBlock - 1) / kBlock;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
-    }
-    mbar_init(cbar, kConsumerWarps * 32);
-    fence_mbar_init();
-  }
   if (threadIdx.x < kRows) {
     const int i = threadIdx.x;
     s_len[i] = (i < nr) ? (p.kv_lens ? p.kv_lens[r0 + i] : p.uniform_len) : 0;
@@ -244,33 +283,36 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == kConsumerWarps) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
       bool abort_flag = false;
       int stage = 0;
       uint32_t phase = 0;
       int fills = 0;
-      for (int b = 0; b < nblk; ++b) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, kDetProdEmpty, abort_flag)) break;
-        uint8_t* st = ring + stage * C::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-        const int t0 = tok_begin + b * kBlock;
+      for (int sp = s_begin; sp < s_end && !abort_flag; ++sp) {
+        const int tb = sp * kSplit;
+        const int nblk = (min(tb + kSplit, max_len) - tb + kBlock - 1) / kBlock;
+        for (int b = 0; b < nblk; ++b) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, kDetProdEmpty, abort_flag)) break;
+          uint8_t* st = ring + stage * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          const int t0 = tb + b * kBlock;
 #pragma unroll
-        for (int bx = 0; bx < C::NBOX; ++bx) {
-          tma_load_4d(st + bx * C::BOX_BYTES, &tmK, &full[stage], bx * C::BOXD, t0, kvh, seq);
-          tma_load_4d(st + C::TENSOR_BYTES + bx * C::BOX_BYTES, &tmV, &full[stage], bx * C::BOXD, t0, kvh, seq);
-        }
-        ++fills;
-        if (++stage == C::STAGES) {
-          stage = 0;
-          phase ^= 1u;
+          for (int bx = 0; bx < C::NBOX; ++bx) {
+            tma_load_4d(st + bx * C::BOX_BYTES, &tmK, &full[stage], bx * C::BOXD, t0, kvh, seq);
+            tma_load_4d(st + C::TENSOR_BYTES + bx * C::BOX_BYTES, &tmV, &full[stage], bx * C::BOXD, t0, kvh,
+                        seq);
+          }
+          ++fills;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
       bool drain_abort = false;
       for (int f = (fills > C::STAGES ? fills - C::STAGES : 0); f < fills; ++f)
         mbar_wait(&full[f % C::STAGES], static_cast<uint32_t>((f / C::STAGES) & 1), kDetDrain, drain_abort);
     }
-    return;  // the producer warp takes no part in the combine
+    return;  // the producer warp takes no part in the merges
   }
 
   // ---------------- consumers ----------------
@@ -280,8 +322,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int rho0 = g, rho1 = g + 8;
   const bool v0 = rho0 < valid_rows, v1 = rho1 < valid_rows;
   const int i0 = v0 ? rho0 / p.G : 0, i1 = v1 ? rho1 / p.G : 0;
-  const int end0 = v0 ? min(s_len[i0], tok_begin + kSplit) : 0;  // row's own token end in this split
-  const int end1 = v1 ? min(s_len[i1], tok_begin + kSplit) : 0;
+  const int ctid = threadIdx.x;  // 0..127
 
   // Q fragments (A operand, rows rho0/rho1), loaded once.
   constexpr int KC = D / 16;
@@ -300,201 +341,231 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
 
-  constexpr int NT = D / 8;  // output n-tiles of 8 along d
-  float o[NT][4];
+  // running split-order merge of the elements this thread owns (direct path)
+  float run_m[KM], run_l[KM], run_o[KM];
 #pragma unroll
-  for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
-  float m_r[2] = {-INFINITY, -INFINITY};
-  float l_r[2] = {0.0f, 0.0f};
+  for (int k = 0; k < KM; ++k) {
+    run_m[k] = -INFINITY;
+    run_l[k] = 0.0f;
+    run_o[k] = 0.0f;
+  }
 
+  constexpr int NT = D / 8;  // output n-tiles of 8 along d
   const int wr = warp * 16;  // this warp's first token row inside a block
+  const int64_t slot = ((int64_t)tile * p.hkv + kvh) * p.max_splits;
   int stage = 0;
   uint32_t phase = 0;
-  for (int b = 0; b < nblk; ++b) {
-    if (!mbar_wait(&full[stage], phase, kDetFull, abort_flag)) break;
-    const uint32_t kbase = smem_u32(ring + stage * C::STAGE_BYTES);
-    const uint32_t vbase = kbase + C::TENSOR_BYTES;
-    const int t0 = tok_begin + b * kBlock + wr;  // token of this warp's row 0
+  uint32_t cphase = 0;
 
-    // Tokens no row of the tile may read: zero their V rows (K is masked by select).
-    const int tile_end = tok_end;
-    if (t0 + 16 > tile_end) {
-      uint8_t* vgen = ring + stage * C::STAGE_BYTES + C::TENSOR_BYTES;
-      for (int e = lane; e < 16 * (D / 8); e += 32) {
-        const int rr = e / (D / 8), c = e % (D / 8);
-        if (t0 + rr >= tile_end) {
-          const uint32_t a = chunk_addr<D>(0u, wr + rr, c);
-          *reinterpret_cast<uint4*>(vgen + a) = make_uint4(0u, 0u, 0u, 0u);
-        }
-      }
-      // order these generic-proxy writes before the next TMA write of the stage
-      fence_proxy_async_smem();
-      __syncwarp();
-    }
+  for (int sp = s_begin; sp < s_end && !abort_flag; ++sp) {
+    const int tok_begin = sp * kSplit;
+    const int tok_end = min(tok_begin + kSplit, max_len);
+    const int nblk = (tok_end - tok_begin + kBlock - 1) / kBlock;
+    const int end0 = v0 ? min(s_len[i0], tok_begin + kSplit) : 0;  // row's own token end in this split
+    const int end1 = v1 ? min(s_len[i1], tok_begin + kSplit) : 0;
 
-    // S = Q K^T for this warp's 16 tokens (two n-tiles of 8 tokens).
-    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+    float o[NT][4];
 #pragma unroll
-    for (int kc = 0; kc < KC; ++kc) {
-      const int mi = lane >> 3, ri = lane & 7;
-      const int r = wr + (mi >> 1) * 8 + ri;
-      const int c = 2 * kc + (mi & 1);
-      uint32_t b00, b01, b10, b11;
-      ldsm_x4(chunk_addr<D>(kbase, r, c), b00, b01, b10, b11);
-      mma16816<T>(s0, qa[kc], b00, b01);
-      mma16816<T>(s1, qa[kc], b10, b11);
+    for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+    float m_r[2] = {-INFINITY, -INFINITY};
+    float l_r[2] = {0.0f, 0.0f};
+
+    for (int b = 0; b < nblk; ++b) {
+      if (!mbar_wait(&full[stage], phase, kDetFull, abort_flag)) break;
+      const uint32_t kbase = smem_u32(ring + stage * C::STAGE_BYTES);
+      const uint32_t vbase = kbase + C::TENSOR_BYTES;
+      const int t0 = tok_begin + b * kBlock + wr;  // token of this warp's row 0
+
+      // Tokens no row of the tile may read: zero their V rows (K is masked by select).
+      if (t0 + 16 > tok_end) {
+        uint8_t* vgen = ring + stage * C::STAGE_BYTES + C::TENSOR_BYTES;
+        for (int e = lane; e < 16 * (D / 8); e += 32) {
+          const int rr = e / (D / 8), c = e % (D / 8);
+          if (t0 + rr >= tok_end) {
+            const uint32_t a = chunk_addr<D>(0u, wr + rr, c);
+            *reinterpret_cast<uint4*>(vgen + a) = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        // order these generic-proxy writes before the next TMA write of the stage
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+
+      // S = Q K^T for this warp's 16 tokens (two n-tiles of 8 tokens).
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kc = 0; kc < KC; ++kc) {
+        const int mi = lane >> 3, ri = lane & 7;
+        const int r = wr + (mi >> 1) * 8 + ri;
+        const int c = 2 * kc + (mi & 1);
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4(chunk_addr<D>(kbase, r, c), b00, b01, b10, b11);
+        mma16816<T>(s0, qa[kc], b00, b01);
+        mma16816<T>(s1, qa[kc], b10, b11);
+      }
+
+      // scale, mask, online softmax update (rows rho0 -> s*[0..1], rho1 -> s*[2..3])
+      const int tk = t0 + 2 * t4;
+      float sc[2][4];
+      sc[0][0] = (tk + 0 < end0) ? __fmul_rn(s0[0], p.scale_log2) : -INFINITY;
+      sc[0][1] = (tk + 1 < end0) ? __fmul_rn(s0[1], p.scale_log2) : -INFINITY;
+      sc[0][2] = (tk + 8 < end0) ? __fmul_rn(s1[0], p.scale_log2) : -INFINITY;
+      sc[0][3] = (tk + 9 < end0) ? __fmul_rn(s1[1], p.scale_log2) : -INFINITY;
+      sc[1][0] = (tk + 0 < end1) ? __fmul_rn(s0[2], p.scale_log2) : -INFINITY;
+      sc[1][1] = (tk + 1 < end1) ? __fmul_rn(s0[3], p.scale_log2) : -INFINITY;
+      sc[1][2] = (tk + 8 < end1) ? __fmul_rn(s1[2], p.scale_log2) : -INFINITY;
+      sc[1][3] = (tk + 9 < end1) ? __fmul_rn(s1[3], p.scale_log2) : -INFINITY;
+
+      uint32_t pa[4];
+      float alpha[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float mx = fmaxf(fmaxf(sc[h][0], sc[h][1]), fmaxf(sc[h][2], sc[h][3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_r[h], mx);
+        const float mref = (m_new == -INFINITY) ? 0.0f : m_new;
+        alpha[h] = weight_of(m_r[h], mref);
+        float pr[4];
+        const uint32_t lo = pack_round<T>(weight_of(sc[h][0], mref), weight_of(sc[h][1], mref), pr[0], pr[1]);
+        const uint32_t hi = pack_round<T>(weight_of(sc[h][2], mref), weight_of(sc[h][3], mref), pr[2], pr[3]);
+        pa[h] = lo;      // a0 (row g) / a1 (row g+8): tokens 2t, 2t+1
+        pa[h + 2] = hi;  // a2 / a3: tokens 8+2t, 8+2t+1
+        const float psum = __fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3]));
+        l_r[h] = __fadd_rn(__fmul_rn(l_r[h], alpha[h]), psum);
+        m_r[h] = m_new;
+      }
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        o[j][0] = __fmul_rn(o[j][0], alpha[0]);
+        o[j][1] = __fmul_rn(o[j][1], alpha[0]);
+        o[j][2] = __fmul_rn(o[j][2], alpha[1]);
+        o[j][3] = __fmul_rn(o[j][3], alpha[1]);
+      }
+      // O += P V
+#pragma unroll
+      for (int pc = 0; pc < D / 16; ++pc) {
+        const int mi = lane >> 3, ri = lane & 7;
+        const int r = wr + (mi & 1) * 8 + ri;
+        const int c = 2 * pc + (mi >> 1);
+        uint32_t b0a, b1a, b0b, b1b;
+        ldsm_x4_t(chunk_addr<D>(vbase, r, c), b0a, b1a, b0b, b1b);
+        mma16816<T>(o[2 * pc], pa, b0a, b1a);
+        mma16816<T>(o[2 * pc + 1], pa, b0b, b1b);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == C::STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
     }
 
-    // scale, mask, online softmax update (rows rho0 -> s*[0..1], rho1 -> s*[2..3])
-    const int tk = t0 + 2 * t4;
-    float sc[2][4];
-    sc[0][0] = (tk + 0 < end0) ? __fmul_rn(s0[0], p.scale_log2) : -INFINITY;
-    sc[0][1] = (tk + 1 < end0) ? __fmul_rn(s0[1], p.scale_log2) : -INFINITY;
-    sc[0][2] = (tk + 8 < end0) ? __fmul_rn(s1[0], p.scale_log2) : -INFINITY;
-    sc[0][3] = (tk + 9 < end0) ? __fmul_rn(s1[1], p.scale_log2) : -INFINITY;
-    sc[1][0] = (tk + 0 < end1) ? __fmul_rn(s0[2], p.scale_log2) : -INFINITY;
-    sc[1][1] = (tk + 1 < end1) ? __fmul_rn(s0[3], p.scale_log2) : -INFINITY;
-    sc[1][2] = (tk + 8 < end1) ? __fmul_rn(s1[2], p.scale_log2) : -INFINITY;
-    sc[1][3] = (tk + 9 < end1) ? __fmul_rn(s1[3], p.scale_log2) : -INFINITY;
-
-    uint32_t pa[4];
-    float alpha[2];
+    // quad-reduce l (fixed butterfly; m is already quad-uniform)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      float mx = fmaxf(fmaxf(sc[h][0], sc[h][1]), fmaxf(sc[h][2], sc[h][3]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_r[h], mx);
-      const float mref = (m_new == -INFINITY) ? 0.0f : m_new;
-      alpha[h] = weight_of(m_r[h], mref);
-      float pr[4];
-      const uint32_t lo = pack_round<T>(weight_of(sc[h][0], mref), weight_of(sc[h][1], mref), pr[0], pr[1]);
-      const uint32_t hi = pack_round<T>(weight_of(sc[h][2], mref), weight_of(sc[h][3], mref), pr[2], pr[3]);
-      pa[h] = lo;      // a0 (row g) / a1 (row g+8): tokens 2t, 2t+1
-      pa[h + 2] = hi;  // a2 / a3: tokens 8+2t, 8+2t+1
-      const float psum = __fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3]));
-      l_r[h] = __fadd_rn(__fmul_rn(l_r[h], alpha[h]), psum);
-      m_r[h] = m_new;
+      l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 1));
+      l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 2));
     }
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      o[j][0] = __fmul_rn(o[j][0], alpha[0]);
-      o[j][1] = __fmul_rn(o[j][1], alpha[0]);
-      o[j][2] = __fmul_rn(o[j][2], alpha[1]);
-      o[j][3] = __fmul_rn(o[j][3], alpha[1]);
-    }
-    // O += P V
-#pragma unroll
-    for (int pc = 0; pc < D / 16; ++pc) {
-      const int mi = lane >> 3, ri = lane & 7;
-      const int r = wr + (mi & 1) * 8 + ri;
-      const int c = 2 * pc + (mi >> 1);
-      uint32_t b0a, b1a, b0b, b1b;
-      ldsm_x4_t(chunk_addr<D>(vbase, r, c), b0a, b1a, b0b, b1b);
-      mma16816<T>(o[2 * pc], pa, b0a, b1a);
-      mma16816<T>(o[2 * pc + 1], pa, b0b, b1b);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[stage]);
-    if (++stage == C::STAGES) {
-      stage = 0;
-      phase ^= 1u;
-    }
-  }
 
-  // quad-reduce l (fixed butterfly; m is already quad-uniform)
+    // ---- merge the four warps of this split in warp order ----
+    if (!csync(cbar, cphase, abort_flag)) break;   // the previous split's merge reads are done
+    if (v0) {
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 1));
-    l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 2));
-  }
+      for (int j = 0; j < NT; ++j)
+        *reinterpret_cast<float2*>(comb_o + (warp * p.rows_cap + rho0) * C::CSTRIDE + j * 8 + 2 * t4) =
+            make_float2(o[j][0], o[j][1]);
+      if (t4 == 0) {
+        comb_ml[(warp * p.rows_cap + rho0) * 2 + 0] = m_r[0];
+        comb_ml[(warp * p.rows_cap + rho0) * 2 + 1] = l_r[0];
+      }
+    }
+    if (v1) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+        *reinterpret_cast<float2*>(comb_o + (warp * p.rows_cap + rho1) * C::CSTRIDE + j * 8 + 2 * t4) =
+            make_float2(o[j][2], o[j][3]);
+      if (t4 == 0) {
+        comb_ml[(warp * p.rows_cap + rho1) * 2 + 0] = m_r[1];
+        comb_ml[(warp * p.rows_cap + rho1) * 2 + 1] = l_r[1];
+      }
+    }
+    if (!csync(cbar, cphase, abort_flag)) break;
 
-  // ---- merge the four warps in warp order ----
-  uint32_t cphase = 0;
-  const int ctid = threadIdx.x;  // 0..127
-  float* comb_o = reinterpret_cast<float*>(ring);                        // [4][16][D]
-  float* comb_ml = comb_o + kConsumerWarps * kRows * D;                  // [4][16][2]
-  csync(cbar, cphase, abort_flag);  // every warp is done reading the ring
-  if (!abort_flag) {
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      const int d = j * 8 + 2 * t4;
-      comb_o[(warp * kRows + rho0) * D + d] = o[j][0];
-      comb_o[(warp * kRows + rho0) * D + d + 1] = o[j][1];
-      comb_o[(warp * kRows + rho1) * D + d] = o[j][2];
-      comb_o[(warp * kRows + rho1) * D + d + 1] = o[j][3];
-    }
-    if (t4 == 0) {
-      comb_ml[(warp * kRows + rho0) * 2 + 0] = m_r[0];
-      comb_ml[(warp * kRows + rho0) * 2 + 1] = l_r[0];
-      comb_ml[(warp * kRows + rho1) * 2 + 0] = m_r[1];
-      comb_ml[(warp * kRows + rho1) * 2 + 1] = l_r[1];
-    }
-  }
-  csync(cbar, cphase, abort_flag);
-  if (abort_flag) return;
-
-  const int64_t slot = ((int64_t)tile * p.hkv + kvh) * p.max_splits;
-  for (int e = ctid; e < valid_rows * D; e += kConsumerWarps * 32) {
-    const int rho = e / D, d = e % D;
-    float mw[kConsumerWarps];
-    float M = -INFINITY;
+    for (int k = 0; k < KM; ++k) {
+      const int e = ctid + k * (kConsumerWarps * 32);
+      if (e < valid_rows * D) {
+        const int rho = e / D, d = e % D;
+        float mw[kConsumerWarps];
+        float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) {
-      mw[w] = comb_ml[(w * kRows + rho) * 2];
-      M = fmaxf(M, mw[w]);
-    }
-    const float mref = (M == -INFINITY) ? 0.0f : M;
-    float L = 0.0f, O = 0.0f;
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          mw[w] = comb_ml[(w * p.rows_cap + rho) * 2];
+          M = fmaxf(M, mw[w]);
+        }
+        const float mref = (M == -INFINITY) ? 0.0f : M;
+        float L = 0.0f, O = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) {
-      const float wt = weight_of(mw[w], mref);
-      L = __fadd_rn(L, __fmul_rn(comb_ml[(w * kRows + rho) * 2 + 1], wt));
-      O = __fadd_rn(O, __fmul_rn(comb_o[(w * kRows + rho) * D + d], wt));
-    }
-    const int i = rho / p.G, gh = rho % p.G;
-    if (nsplits == 1) {
-      const float r = (s_len[i] == 0) ? 0.0f : __fdiv_rn(O, L);
-      out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(r);
-    } else {
-      const int64_t base = (slot + split) * p.rows_cap + rho;
-      p.ws_o[base * D + d] = O;
-      if (d == 0) {
-        p.ws_ml[base * 2 + 0] = M;
-        p.ws_ml[base * 2 + 1] = L;
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float wt = weight_of(mw[w], mref);
+          L = __fadd_rn(L, __fmul_rn(comb_ml[(w * p.rows_cap + rho) * 2 + 1], wt));
+          O = __fadd_rn(O, __fmul_rn(comb_o[(w * p.rows_cap + rho) * C::CSTRIDE + d], wt));
+        }
+        if (direct) {
+          const int own = (s_len[rho / p.G] + kSplit - 1) / kSplit;
+          if (sp < own) merge_split(sp == 0, run_m[k], run_l[k], run_o[k], M, L, O);
+        } else {
+          const int64_t base = (slot + sp) * p.rows_cap + rho;
+          p.ws_o[base * D + d] = O;
+          if (d == 0) {
+            p.ws_ml[base * 2 + 0] = M;
+            p.ws_ml[base * 2 + 1] = L;
+          }
+        }
       }
     }
   }
-  if (nsplits == 1) return;
+  if (abort_flag) return;
 
-  // ---- cross-split combine by the last CTA of this (tile, kv head) ----
-  __threadfence();
-  if (!csync(cbar, cphase, abort_flag)) return;
-  if (ctid == 0) {
-    const int old = atomicAdd(p.counters + (int64_t)tile * p.hkv + kvh, 1);
-    const bool last = (old == nsplits - 1);
-    s_misc[0] = last ? 1 : 0;
-    if (last) p.counters[(int64_t)tile * p.hkv + kvh] = 0;
-  }
-  if (!csync(cbar, cphase, abort_flag)) return;
-  if (s_misc[0] == 0) return;
-  __threadfence();
-  for (int e = ctid; e < valid_rows * D; e += kConsumerWarps * 32) {
-    const int rho = e / D, d = e % D;
-    const int i = rho / p.G, gh = rho % p.G;
-    const int own = (s_len[i] + kSplit - 1) / kSplit;  // this row's own split count
-    float M = -INFINITY;
-    for (int s = 0; s < own; ++s) M = fmaxf(M, __ldcg(p.ws_ml + ((slot + s) * p.rows_cap + rho) * 2));
-    const float mref = (M == -INFINITY) ? 0.0f : M;
-    float L = 0.0f, O = 0.0f;
-    for (int s = 0; s < own; ++s) {
-      const int64_t base = (slot + s) * p.rows_cap + rho;
-      const float wt = weight_of(__ldcg(p.ws_ml + base * 2), mref);
-      L = __fadd_rn(L, __fmul_rn(__ldcg(p.ws_ml + base * 2 + 1), wt));
-      O = __fadd_rn(O, __fmul_rn(__ldcg(p.ws_o + base * D + d), wt));
+  if (!direct) {
+    // ---- the last CTA of this (tile, kv head) replays the split-order merge ----
+    __threadfence();
+    if (!csync(cbar, cphase, abort_flag)) return;
+    if (ctid == 0) {
+      const int arrivals = (nsplits + p.spu - 1) / p.spu;
+      const int old = atomicAdd(p.counters + (int64_t)tile * p.hkv + kvh, 1);
+      const bool last = (old == arrivals - 1);
+      s_misc[0] = last ? 1 : 0;
+      if (last) p.counters[(int64_t)tile * p.hkv + kvh] = 0;
     }
-    const float r = (own == 0) ? 0.0f : __fdiv_rn(O, L);
-    out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(r);
+    if (!csync(cbar, cphase, abort_flag)) return;
+    if (s_misc[0] == 0) return;
+    __threadfence();
+#pragma unroll
+    for (int k = 0; k < KM; ++k) {
+      const int e = ctid + k * (kConsumerWarps * 32);
+      if (e < valid_rows * D) {
+        const int rho = e / D, d = e % D;
+        const int own = (s_len[rho / p.G] + kSplit - 1) / kSplit;
+        for (int s = 0; s < own; ++s) {
+          const int64_t base = (slot + s) * p.rows_cap + rho;
+          merge_split(s == 0, run_m[k], run_l[k], run_o[k], __ldcg(p.ws_ml + base * 2), __ldcg(p.ws_ml + base * 2 + 1),
+                      __ldcg(p.ws_o + base * D + d));
+        }
+      }
+    }
+  }
+
+#pragma unroll
+  for (int k = 0; k < KM; ++k) {
+    const int e = ctid + k * (kConsumerWarps * 32);
+    if (e < valid_rows * D) {
+      const int rho = e / D, d = e % D;
+      const int i = rho / p.G, gh = rho % p.G;
+      const float r = (s_len[i] == 0) ? 0.0f : __fdiv_rn(run_o[k], run_l[k]);
+      out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(r);
+    }
   }
 }
 

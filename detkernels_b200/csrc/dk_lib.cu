@@ -345,10 +345,13 @@ int launch_cast(const float* src, void* c, int64_t ldc, int M, int N, cudaStream
 
 // ============================ attention ============================
 struct AttnPlan {
-  int n_tiles, rows_cap, max_splits;
+  int n_tiles, rows_cap, max_splits, spu, upt;
   size_t o_bytes, ml_bytes, cnt_bytes, total;
 };
 
+// Splits per CTA (schedule only; the arithmetic of a row never depends on it):
+// enough CTAs to fill the GPU a few times over, at most 8 splits (2048 tokens)
+// per CTA so long rows do not leave a tail.
 AttnPlan plan_attention(int32_t n_tiles, int32_t rows_per_tile, int32_t hq, int32_t hkv, int32_t D,
                         int32_t max_kv_len) {
   AttnPlan pl{};
@@ -356,25 +359,45 @@ AttnPlan plan_attention(int32_t n_tiles, int32_t rows_per_tile, int32_t hq, int3
   pl.n_tiles = n_tiles;
   pl.rows_cap = (rows_per_tile <= 1) ? G : (dk::attn::kRows / G) * G;
   pl.max_splits = static_cast<int>(ceil_div(max_kv_len > 0 ? max_kv_len : 1, dk::attn::kSplit));
+  const int64_t pairs = static_cast<int64_t>(n_tiles) * (hkv > 0 ? hkv : 1);
+  const int64_t target = 4LL * sm_count(current_device());
+  int64_t upt = (pairs >= target) ? 1 : ceil_div(target, pairs);
+  if (upt > pl.max_splits) upt = pl.max_splits;
+  int spu = static_cast<int>(ceil_div(pl.max_splits, upt));
+  if (spu > 8) spu = 8;
+  if (spu < 1) spu = 1;
+  pl.spu = spu;
+  pl.upt = static_cast<int>(ceil_div(pl.max_splits, spu));
   const size_t slots = static_cast<size_t>(n_tiles) * hkv * pl.max_splits * pl.rows_cap;
   pl.o_bytes = ceil_div(slots * D * sizeof(float), 256) * 256;
   pl.ml_bytes = ceil_div(slots * 2 * sizeof(float), 256) * 256;
   pl.cnt_bytes = static_cast<size_t>(n_tiles) * hkv * sizeof(int32_t);
-  // only multi-split work needs scratch; single-split rows write the output directly
-  pl.total = (pl.max_splits > 1) ? (kCounterBytes + pl.o_bytes + pl.ml_bytes) : 0;
+  // scratch only when some tile's splits are spread over several CTAs
+  pl.total = (pl.upt > 1) ? (kCounterBytes + pl.o_bytes + pl.ml_bytes) : 0;
   return pl;
+}
+
+template <typename T, int D, int KM>
+int attn_launch_km(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int grid_x, int grid_y,
+                   cudaStream_t st) {
+  using C = dk::attn::Cfg<D>;
+  static bool done[kMaxDevices] = {false};
+  auto fn = dk::attn::attn_kernel<T, D, KM>;
+  int rc = ensure_smem(fn, C::smem_bytes(dk::attn::kRows), done);
+  if (rc) return rc;
+  cudaError_t e = launch_pdl(fn, dim3(grid_x, grid_y), dim3(dk::attn::kThreads), C::smem_bytes(p.rows_cap), st, tk,
+                             tv, p);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "attention_batch_invariant: launch failed: %s", cudaGetErrorString(e));
+  return DK_OK;
 }
 
 template <typename T, int D>
 int attn_launch(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int grid_x, int grid_y,
                 cudaStream_t st) {
-  using C = dk::attn::Cfg<D>;
-  static bool done[kMaxDevices] = {false};
-  auto fn = dk::attn::attn_kernel<T, D>;
-  int rc = ensure_smem(fn, C::SMEM_BYTES, done);
-  if (rc) return rc;
-  fn<<<dim3(grid_x, grid_y), dk::attn::kThreads, C::SMEM_BYTES, st>>>(tk, tv, p);
-  return check_launch("attention_batch_invariant");
+  constexpr int kThr = dk::attn::kConsumerWarps * 32;
+  constexpr int kNarrow = (4 < dk::attn::Cfg<D>::KMAX) ? 4 : dk::attn::Cfg<D>::KMAX;
+  if (p.rows_cap * D <= kNarrow * kThr) return attn_launch_km<T, D, kNarrow>(tk, tv, p, grid_x, grid_y, st);
+  return attn_launch_km<T, D, dk::attn::Cfg<D>::KMAX>(tk, tv, p, grid_x, grid_y, st);
 }
 
 }  // namespace
@@ -439,8 +462,8 @@ int dk_kernel_attributes(int which, int* num_regs, int* max_threads, int* local_
   cudaError_t e;
   switch (which) {
     case 0: e = cudaFuncGetAttributes(&a, dk::gemm::gemm_kernel<__nv_bfloat16, 1>); break;
-    case 1: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 128>); break;
-    case 2: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 64>); break;
+    case 1: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 128, 4>); break;
+    case 2: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 64, 4>); break;
     case 3: e = cudaFuncGetAttributes(&a, dk::rmsnorm_inv_vec_kernel<float, float, 8>); break;
     default: return fail(DK_ERR_INVALID_ARGUMENT, "dk_kernel_attributes: unknown kernel %d", which);
   }
@@ -668,7 +691,7 @@ int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_
     return fail(DK_ERR_INVALID_ARGUMENT, "%s: q rows must be 4-byte aligned", what);
 
   const AttnPlan pl = plan_attention(n_tiles, row_tiles ? 2 : 1, n_q_heads, n_kv_heads, head_dim, max_kv_len);
-  if (static_cast<int64_t>(pl.n_tiles) * pl.max_splits > 0x7fffffffLL)
+  if (static_cast<int64_t>(pl.n_tiles) * pl.upt > 0x7fffffffLL)
     return fail(DK_ERR_INVALID_ARGUMENT, "%s: grid too large", what);
   if (pl.total > 0 && (!workspace || workspace_bytes < pl.total))
     return fail(DK_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", what, pl.total, workspace_bytes);
@@ -691,6 +714,8 @@ int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_
   p.hkv = n_kv_heads;
   p.G = G;
   p.max_splits = pl.max_splits;
+  p.spu = pl.spu;
+  p.upt = pl.upt;
   p.kv_capacity = static_cast<int32_t>(kv_capacity);
   p.kv_n_seq = static_cast<int32_t>(kv_n_seq);
   p.scale_log2 = scale * 1.4426950408889634f;
@@ -720,7 +745,7 @@ int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_
   if (rc) return rc;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int gx = pl.n_tiles * pl.max_splits;
+  const int gx = pl.n_tiles * pl.upt;
   const int gy = n_kv_heads;
   if (dtype == DK_BF16) {
     if (head_dim == 32) return attn_launch<__nv_bfloat16, 32>(tk, tv, p, gx, gy, st);

@@ -66,7 +66,7 @@ int dk_device_status(int device, int clear, int* code, int* detail);
 int dk_num_sms(int device, int* out);
 /* Introspection of the compiled kernels on the current device (registers per thread, the
  * launch-time thread limit, local-memory bytes, dynamic shared-memory limit).  which: 0 = bf16
- * GEMM, 1 = bf16 attention d128, 2 = bf16 attention d64, 3 = f32 RMSNorm. */
+ * GEMM, 1 = bf16 decode attention d128, 2 = bf16 decode attention d64, 3 = f32 RMSNorm. */
 int dk_kernel_attributes(int which, int* num_regs, int* max_threads, int* local_bytes, int* max_dynamic_smem);
 
 /* ---- RMSNorm: y = x * rsqrt(mean(x^2) + eps) * w, f32 math, y in x's dtype ----
