@@ -51,6 +51,9 @@ SIGNATURES = {
     "dk_matmul_workspace_size": (_size, [_i64, _i64, _i64]),
     "dk_matmul_batch_invariant": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _i64, _int,
                                          _c_void_p, _size, _c_void_p]),
+    "dk_matmul_batch_invariant_ex": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _i64,
+                                            _int, _c_void_p, _c_void_p, _size, _c_void_p]),
+    "dk_argmax_finish": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "dk_matmul_slice_partials": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _int, _int,
                                         _int, _c_void_p]),
     "dk_matmul_fold_slices": (_int, [_c_void_p, _int, _c_void_p, _i64, _i64, _i64, _int, _c_void_p]),
@@ -70,6 +73,24 @@ SIGNATURES = {
                                           _i64, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _int, _c_void_p, _size,
                                           _c_void_p]),
 }
+
+
+DK_EPI_STORE = 0
+DK_EPI_RESIDUAL = 1
+DK_EPI_SILU = 2
+DK_EPI_SILU_MUL = 3
+DK_EPI_QKV_CACHE = 4
+DK_EPI_ARGMAX = 5
+
+
+class MatmulEpilogue(ctypes.Structure):
+    """ctypes mirror of dk_matmul_epilogue."""
+    _fields_ = [("mode", ctypes.c_int), ("resid", ctypes.c_void_p), ("ld_resid", ctypes.c_int64),
+                ("q_cols", ctypes.c_int32), ("kv_cols", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+                ("cache_stride_seq", ctypes.c_int64), ("cache_stride_head", ctypes.c_int64),
+                ("cache_stride_tok", ctypes.c_int64), ("row_seq", ctypes.c_void_p), ("row_pos", ctypes.c_void_p),
+                ("argmax_keys", ctypes.c_void_p)]
 
 
 class DetKernelsError(RuntimeError):

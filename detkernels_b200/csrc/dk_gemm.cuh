@@ -100,6 +100,7 @@ __host__ __device__ __forceinline__ int slot_of(int i, int unit_ordinal, int gro
 enum Mode : int { FOLD = 0, SPLIT = 1, PARTIAL = 2, ATOMIC = 3 };
 
 struct Params {
+  dk_matmul_epilogue epi;        // what is done with each final value (DK_EPI_*)
   int M, N, K;
   int slice_len;                 // elements per slice (multiple of 16)
   int slice_begin, slice_end;    // slices computed by this launch
@@ -136,15 +137,119 @@ __device__ __forceinline__ float tree_sum(const float* v, int n) {
                    __fadd_rn(__fadd_rn(v[4], v[5]), __fadd_rn(v[6], v[7])));
 }
 
+__device__ __forceinline__ float silu_f32(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+
+template <typename T>
+__device__ __forceinline__ float rnd(float v) {
+  return to_f32<T>(from_f32<T>(v));
+}
+
+// Final value v of output element (m, n) -> memory, per the epilogue mode (all but SILU_MUL).
+template <typename T>
+__device__ __forceinline__ void store_final(const Params& p, T* C, int m, int n, float v) {
+  const dk_matmul_epilogue& e = p.epi;
+  switch (e.mode) {
+    case DK_EPI_RESIDUAL: {
+      const float r = to_f32<T>(static_cast<const T*>(e.resid)[static_cast<int64_t>(m) * e.ld_resid + n]);
+      C[static_cast<int64_t>(m) * p.ldc + n] = from_f32<T>(__fadd_rn(r, rnd<T>(v)));
+      break;
+    }
+    case DK_EPI_SILU:
+      C[static_cast<int64_t>(m) * p.ldc + n] = from_f32<T>(silu_f32(rnd<T>(v)));
+      break;
+    case DK_EPI_QKV_CACHE: {
+      if (n < e.q_cols) {
+        C[static_cast<int64_t>(m) * p.ldc + n] = from_f32<T>(v);
+      } else {
+        const int j = n - e.q_cols;
+        const int which = j / e.kv_cols;
+        const int jj = j - which * e.kv_cols;
+        const int head = jj / e.head_dim, d = jj - head * e.head_dim;
+        const int64_t seq = e.row_seq ? e.row_seq[m] : m;
+        T* cache = static_cast<T*>(which == 0 ? e.k_cache : e.v_cache);
+        cache[seq * e.cache_stride_seq + head * e.cache_stride_head +
+              static_cast<int64_t>(e.row_pos[m]) * e.cache_stride_tok + d] = from_f32<T>(v);
+      }
+      break;
+    }
+    default:
+      C[static_cast<int64_t>(m) * p.ldc + n] = from_f32<T>(v);
+  }
+}
+
+// Argmax key of the rounded value v at column n: larger key = larger value, and among equal values
+// the smaller column.  NaN sorts above everything; -0 and +0 are equal.  Every real key is > 0.
+template <typename T>
+__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
+  const float r = rnd<T>(v);
+  uint32_t hi;
+  if (r != r) {
+    hi = 0xffffffffu;
+  } else {
+    const uint32_t b = __float_as_uint(r == 0.0f ? 0.0f : r);
+    hi = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  }
+  return (static_cast<unsigned long long>(hi) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(n));
+}
+
+// Max over the 32 lanes (columns) of each of 32 token values k[0..31]; lane L ends with token L's
+// maximum in k[0].  Reduce-scatter butterfly: 31 exchanges instead of 32 x 5.
+__device__ __forceinline__ unsigned long long warp_max_scatter(unsigned long long (&k)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool upper = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const unsigned long long send = upper ? k[i] : k[i + w];
+      const unsigned long long keep = upper ? k[i + w] : k[i];
+      const unsigned long long recv = __shfl_xor_sync(0xffffffffu, send, w);
+      k[i] = keep > recv ? keep : recv;
+    }
+  }
+  return k[0];
+}
+
+// gate value g (column 2j) and up value u (column 2j+1) -> C[m, j]
+template <typename T>
+__device__ __forceinline__ void store_silu_mul(const Params& p, T* C, int m, int j, float g, float u) {
+  const float s = rnd<T>(silu_f32(rnd<T>(g)));
+  C[static_cast<int64_t>(m) * p.ldc + j] = from_f32<T>(__fmul_rn(s, rnd<T>(u)));
+}
+
+// Thread <-> column n (consecutive columns in consecutive lanes), 32 tokens from m_first.
+// Every lane of the warp calls this (the gate/up exchange is a shuffle).
 template <typename T>
 __device__ __forceinline__ void emit_chunk(const Params& p, T* C, int mode, int n, bool n_ok, int m_first,
                                            const float (&t)[32]) {
+  if (mode == FOLD && p.epi.mode == DK_EPI_ARGMAX) {
+    unsigned long long k[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int m = m_first + j;
+      k[j] = (n_ok && m < p.M) ? argmax_key<T>(t[j], n) : 0ull;
+      if (n_ok && m < p.M && C) C[static_cast<int64_t>(m) * p.ldc + n] = from_f32<T>(t[j]);
+    }
+    const unsigned long long best = warp_max_scatter(k);
+    const int m = m_first + (threadIdx.x & 31);
+    if (best != 0ull && m < p.M) atomicMax(p.epi.argmax_keys + m, best);
+    return;
+  }
+  if (mode == FOLD && p.epi.mode == DK_EPI_SILU_MUL) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float partner = __shfl_xor_sync(0xffffffffu, t[j], 1);
+      const int m = m_first + j;
+      if (n_ok && (n & 1) == 0 && m < p.M) store_silu_mul<T>(p, C, m, n >> 1, t[j], partner);
+    }
+    return;
+  }
   if (!n_ok) return;
   if (mode == FOLD) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int m = m_first + j;
-      if (m < p.M) C[static_cast<int64_t>(m) * p.ldc + n] = from_f32<T>(t[j]);
+      if (m < p.M) store_final<T>(p, C, m, n, t[j]);
     }
   } else if (mode == ATOMIC) {
 #pragma unroll
@@ -411,9 +516,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // the GEMM) and for the row-parallel TP combine.  Each thread sums 4
 // consecutive columns with 16-byte loads when N allows.
 template <typename T>
-__global__ void __launch_bounds__(256) fold_groups_kernel(const float* __restrict__ partials, int n_parts,
-                                                          T* __restrict__ c, int64_t ldc, int M, int N) {
+__global__ void __launch_bounds__(256) fold_groups_kernel(const float* __restrict__ partials, int n_parts, const Params p) {
   pdl_wait();
+  const int M = p.M, N = p.N;
+  T* c = static_cast<T*>(p.c);
   const int64_t MN = static_cast<int64_t>(M) * N;
   const int64_t quads = (static_cast<int64_t>(N) + 3) / 4;
   const int64_t total = static_cast<int64_t>(M) * quads;
@@ -442,15 +548,50 @@ __global__ void __launch_bounds__(256) fold_groups_kernel(const float* __restric
         for (int e = 0; e < 4; ++e) v[j][e] = 0.0f;
       }
     }
+    float fin[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      if (n0 + e < N) {
-        float col[kSlices];
+      float col[kSlices];
 #pragma unroll
-        for (int j = 0; j < kSlices; ++j) col[j] = v[j][e];
-        c[m * ldc + n0 + e] = from_f32<T>(tree_sum(col, n_parts));
-      }
+      for (int j = 0; j < kSlices; ++j) col[j] = v[j][e];
+      fin[e] = tree_sum(col, n_parts);
     }
+    if (p.epi.mode == DK_EPI_ARGMAX) {
+      unsigned long long best = 0ull;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (n0 + e < N) {
+          const unsigned long long key = argmax_key<T>(fin[e], n0 + e);
+          best = key > best ? key : best;
+          if (c) c[m * p.ldc + n0 + e] = from_f32<T>(fin[e]);
+        }
+      }
+      atomicMax(p.epi.argmax_keys + m, best);
+    } else if (p.epi.mode == DK_EPI_SILU_MUL) {
+      // n0 is a multiple of 4: pairs (n0, n0+1) and (n0+2, n0+3); N is even
+      if (n0 + 1 < N) store_silu_mul<T>(p, c, static_cast<int>(m), n0 >> 1, fin[0], fin[1]);
+      if (n0 + 3 < N) store_silu_mul<T>(p, c, static_cast<int>(m), (n0 >> 1) + 1, fin[2], fin[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (n0 + e < N) store_final<T>(p, c, static_cast<int>(m), n0 + e, fin[e]);
+    }
+  }
+}
+
+// keys[r] -> tokens[r] (column = ~low word), keys reset, lengths advanced.
+__global__ void argmax_finish_kernel(unsigned long long* __restrict__ keys, int64_t n_rows, int64_t* tokens,
+                                     int64_t* tokens_copy, int32_t* lens_a, int32_t* lens_b) {
+  pdl_wait();
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < n_rows;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const unsigned long long k = keys[r];
+    const int64_t col = static_cast<int64_t>(~static_cast<uint32_t>(k & 0xffffffffull));
+    tokens[r] = col;
+    if (tokens_copy) tokens_copy[r] = col;
+    keys[r] = 0ull;
+    if (lens_a) lens_a[r] += 1;
+    if (lens_b) lens_b[r] += 1;
   }
 }
 

@@ -275,12 +275,12 @@ int gemm_validate(const void* a, int64_t lda, const void* b, int64_t ldb, int64_
 }
 
 template <typename T>
-int launch_fold(const float* partials, int n_parts, void* c, int64_t ldc, int M, int N, cudaStream_t st) {
-  const int64_t total = static_cast<int64_t>(M) * ceil_div(N, 4);
+int launch_fold(const float* partials, int n_parts, const dk::gemm::Params& p, cudaStream_t st) {
+  const int64_t total = static_cast<int64_t>(p.M) * ceil_div(p.N, 4);
   const int64_t want = ceil_div(total, 256);
   const int blocks = static_cast<int>(want < 8 * 148 ? want : 8 * 148);
   cudaError_t e = launch_pdl(dk::gemm::fold_groups_kernel<T>, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, st,
-                             partials, n_parts, static_cast<T*>(c), ldc, M, N);
+                             partials, n_parts, p);
   if (e != cudaSuccess) return fail(DK_ERR_CUDA, "matmul fold: launch failed: %s", cudaGetErrorString(e));
   return DK_OK;
 }
@@ -322,8 +322,8 @@ int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ld
   if (p.mode == dk::gemm::SPLIT) {
     // the upper tree levels over the groups' subtree sums, as a dependent launch
     const int n_parts = (p.slice_end - p.slice_begin) / p.group;
-    if (dtype == DK_BF16) return launch_fold<__nv_bfloat16>(p.ws, n_parts, p.c, p.ldc, p.M, p.N, st);
-    return launch_fold<__half>(p.ws, n_parts, p.c, p.ldc, p.M, p.N, st);
+    if (dtype == DK_BF16) return launch_fold<__nv_bfloat16>(p.ws, n_parts, p, st);
+    return launch_fold<__half>(p.ws, n_parts, p, st);
   }
   return check_launch(what);
 }
@@ -533,16 +533,56 @@ size_t dk_matmul_variant_workspace_size(int64_t M, int64_t N) {
 int dk_matmul_batch_invariant(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc, int64_t M,
                               int64_t N, int64_t K, int dtype, void* workspace, size_t workspace_bytes,
                               void* stream) {
+  return dk_matmul_batch_invariant_ex(a, lda, b, ldb, c, ldc, M, N, K, dtype, nullptr, workspace, workspace_bytes,
+                                      stream);
+}
+
+int dk_matmul_batch_invariant_ex(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+                                 int64_t M, int64_t N, int64_t K, int dtype, const dk_matmul_epilogue* epi,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
   const char* what = "matmul_batch_invariant";
   int rc = gemm_validate(a, lda, b, ldb, M, N, K, dtype, what);
   if (rc) return rc;
   if (M == 0 || N == 0) return DK_OK;
-  if (!c) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null output", what);
-  if (ldc < N) return fail(DK_ERR_INVALID_ARGUMENT, "%s: ldc < N", what);
+  dk_matmul_epilogue e{};
+  e.mode = DK_EPI_STORE;
+  if (epi) e = *epi;
+  int64_t out_cols = N;
+  switch (e.mode) {
+    case DK_EPI_STORE:
+    case DK_EPI_SILU:
+      break;
+    case DK_EPI_RESIDUAL:
+      if (!e.resid || e.ld_resid < N) return fail(DK_ERR_INVALID_ARGUMENT, "%s: residual epilogue needs R", what);
+      break;
+    case DK_EPI_SILU_MUL:
+      if (N % 2) return fail(DK_ERR_INVALID_ARGUMENT, "%s: gate/up epilogue needs an even N", what);
+      out_cols = N / 2;
+      break;
+    case DK_EPI_ARGMAX:
+      if (!e.argmax_keys) return fail(DK_ERR_INVALID_ARGUMENT, "%s: argmax epilogue needs keys", what);
+      if (N > 0x7fffffffLL) return fail(DK_ERR_UNSUPPORTED, "%s: argmax over more than 2^31 columns", what);
+      if (!c) out_cols = 0;
+      break;
+    case DK_EPI_QKV_CACHE:
+      if (e.q_cols < 0 || e.kv_cols <= 0 || e.head_dim <= 0 || e.kv_cols % e.head_dim ||
+          static_cast<int64_t>(e.q_cols) + 2LL * e.kv_cols != N || !e.k_cache || !e.v_cache || !e.row_pos)
+        return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad QKV cache epilogue", what);
+      out_cols = e.q_cols;
+      break;
+    default:
+      return fail(DK_ERR_INVALID_ARGUMENT, "%s: unknown epilogue mode %d", what, e.mode);
+  }
+  if (!c && out_cols > 0) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null output", what);
+  if (ldc < out_cols) return fail(DK_ERR_INVALID_ARGUMENT, "%s: ldc too small", what);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (K == 0) return zero_output(c, ldc, M, N, 2, st);
+  if (K == 0) {
+    if (e.mode != DK_EPI_STORE) return fail(DK_ERR_UNSUPPORTED, "%s: K == 0 with a fused epilogue", what);
+    return zero_output(c, ldc, M, N, 2, st);
+  }
   const GemmPlan pl = plan_invariant(M, N, K, sm_count(current_device()));
   dk::gemm::Params p{};
+  p.epi = e;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
@@ -563,6 +603,19 @@ int dk_matmul_batch_invariant(const void* a, int64_t lda, const void* b, int64_t
     p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.partials_off);
   }
   return gemm_launch(dtype, a, lda, b, ldb, p, st, what);
+}
+
+int dk_argmax_finish(unsigned long long* keys, int64_t n_rows, int64_t* tokens, int64_t* tokens_copy,
+                     int32_t* lens_a, int32_t* lens_b, void* stream) {
+  if (n_rows < 0) return fail(DK_ERR_INVALID_ARGUMENT, "argmax_finish: negative row count");
+  if (n_rows == 0) return DK_OK;
+  if (!keys || !tokens) return fail(DK_ERR_INVALID_ARGUMENT, "argmax_finish: null keys or tokens");
+  const int64_t want = ceil_div(n_rows, 256);
+  const int blocks = static_cast<int>(want < 1024 ? want : 1024);
+  cudaError_t e = launch_pdl(dk::gemm::argmax_finish_kernel, dim3(blocks), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), keys, n_rows, tokens, tokens_copy, lens_a, lens_b);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "argmax_finish: launch failed: %s", cudaGetErrorString(e));
+  return DK_OK;
 }
 
 int dk_matmul_slice_partials(const void* a, int64_t lda, const void* b, int64_t ldb, float* partials, int64_t M,
@@ -608,8 +661,14 @@ int dk_matmul_fold_slices(const float* partials, int n_parts, void* c, int64_t l
   if (M == 0 || N == 0) return DK_OK;
   if (!partials || !c || ldc < N) return fail(DK_ERR_INVALID_ARGUMENT, "matmul_fold_slices: bad pointer/ldc");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == DK_BF16) return launch_fold<__nv_bfloat16>(partials, n_parts, c, ldc, (int)M, (int)N, st);
-  return launch_fold<__half>(partials, n_parts, c, ldc, (int)M, (int)N, st);
+  dk::gemm::Params p{};
+  p.epi.mode = DK_EPI_STORE;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.c = c;
+  p.ldc = ldc;
+  if (dtype == DK_BF16) return launch_fold<__nv_bfloat16>(partials, n_parts, p, st);
+  return launch_fold<__half>(partials, n_parts, p, st);
 }
 
 int dk_matmul_batch_variant(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc, int64_t M,

@@ -144,3 +144,100 @@ def matmul_fold_slices(partials, dtype, out=None):
     _lib.check(rc, "matmul_fold_slices")
     _lib.count_launch()
     return out
+
+
+_EPILOGUES = {"store": _lib.DK_EPI_STORE, "residual": _lib.DK_EPI_RESIDUAL, "silu": _lib.DK_EPI_SILU,
+              "silu_mul": _lib.DK_EPI_SILU_MUL, "qkv_cache": _lib.DK_EPI_QKV_CACHE, "argmax": _lib.DK_EPI_ARGMAX}
+
+
+def matmul_fused(a, b, epilogue: str = "store", out=None, workspace=None, residual=None, q_cols: int = 0,
+                 head_dim: int = 0, k_cache=None, v_cache=None, row_seq=None, row_pos=None, argmax_keys=None):
+    """``matmul_batch_invariant`` (same K numerics) with the decoder's next element-wise op fused
+    into the store; every step rounds where the unfused torch sequence rounds, so the result bits
+    equal that sequence's.  Epilogues:
+
+    * ``"store"``: ``a @ b``.
+    * ``"residual"``: ``residual + a @ b`` (``residual`` [M, N]; may be ``out`` itself).
+    * ``"silu"``: ``silu(a @ b)``.
+    * ``"silu_mul"``: b's columns are (gate, up) pairs; returns ``silu(g) * u``, [M, N/2].
+    * ``"qkv_cache"``: the first ``q_cols`` columns are returned ([M, q_cols]); the next
+      (N - q_cols)/2 are K, the last (N - q_cols)/2 are V, written into ``k_cache``/``v_cache``
+      ([n_seq, H_kv, capacity, head_dim]) at sequence ``row_seq[m]`` (int32; None: m) and position
+      ``row_pos[m]`` (int32).
+    * ``"argmax"``: folds each row's first maximal column into ``argmax_keys`` (int64 [M] used as
+      uint64, zero before the call; ``argmax_finish`` reads and re-zeroes them).  Logits are stored
+      only when ``out`` is given.
+    """
+    import ctypes
+
+    import torch
+
+    M, K, N = _check_inputs(a, b, "matmul_fused")
+    if epilogue not in _EPILOGUES:
+        raise ValueError("unknown epilogue %r" % (epilogue,))
+    epi = _lib.MatmulEpilogue()
+    epi.mode = _EPILOGUES[epilogue]
+    out_cols = N
+    if epilogue == "residual":
+        assert residual is not None and residual.shape == (M, N) and residual.dtype == a.dtype
+        assert residual.is_cuda and residual.stride(1) == 1
+        epi.resid, epi.ld_resid = residual.data_ptr(), residual.stride(0)
+    elif epilogue == "silu_mul":
+        if N % 2:
+            raise ValueError("silu_mul needs an even number of columns")
+        out_cols = N // 2
+    elif epilogue == "qkv_cache":
+        kv_cols = (N - q_cols) // 2
+        assert k_cache is not None and v_cache is not None and row_pos is not None
+        assert k_cache.shape == v_cache.shape and k_cache.stride() == v_cache.stride()
+        assert k_cache.dtype == a.dtype and k_cache.stride(3) == 1 and k_cache.shape[3] == head_dim
+        assert row_pos.dtype == torch.int32 and row_pos.numel() >= M
+        assert row_seq is None or (row_seq.dtype == torch.int32 and row_seq.numel() >= M)
+        epi.q_cols, epi.kv_cols, epi.head_dim = int(q_cols), int(kv_cols), int(head_dim)
+        epi.k_cache, epi.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+        epi.cache_stride_seq, epi.cache_stride_head, epi.cache_stride_tok = k_cache.stride(0), k_cache.stride(1), \
+            k_cache.stride(2)
+        epi.row_seq = row_seq.data_ptr() if row_seq is not None else None
+        epi.row_pos = row_pos.data_ptr()
+        out_cols = q_cols
+    elif epilogue == "argmax":
+        assert argmax_keys is not None and argmax_keys.dtype == torch.int64 and argmax_keys.numel() >= M
+        epi.argmax_keys = argmax_keys.data_ptr()
+    if out is None and epilogue != "argmax":
+        out = torch.empty((M, out_cols), device=a.device, dtype=a.dtype)
+    if out is not None:
+        assert out.shape == (M, out_cols) and out.dtype == a.dtype and out.stride(1) == 1
+    if M == 0 or N == 0:
+        return out
+    a2, b2 = _tma_ready(a), _tma_ready(b)
+    lib = _lib.load()
+    stream = _lib.stream_ptr(a.device)
+    if workspace is None:
+        workspace = _lib.workspace(lib.dk_matmul_workspace_size(M, N, K), a.device, stream)
+    rc = lib.dk_matmul_batch_invariant_ex(
+        a2.data_ptr(), a2.stride(0), b2.data_ptr(), b2.stride(0), out.data_ptr() if out is not None else None,
+        out.stride(0) if out is not None else out_cols, M, N, K, _lib.dtype_code(a.dtype), ctypes.byref(epi),
+        workspace.data_ptr() if workspace is not None else None, workspace.numel() if workspace is not None else 0,
+        stream)
+    _lib.check(rc, "matmul_fused")
+    _lib.count_launch()
+    return out
+
+
+def argmax_finish(argmax_keys, tokens, tokens_copy=None, lens_a=None, lens_b=None):
+    """After an ``"argmax"`` matmul over n rows: tokens[r] (int64) = row r's argmax column (also
+    into tokens_copy), keys re-zeroed, lens_a/lens_b (int32) advanced by one."""
+    import torch
+
+    n = tokens.numel()
+    assert argmax_keys.numel() >= n and tokens.dtype == torch.int64 and tokens.is_contiguous()
+    for t in (lens_a, lens_b):
+        assert t is None or (t.dtype == torch.int32 and t.numel() >= n)
+    assert tokens_copy is None or (tokens_copy.dtype == torch.int64 and tokens_copy.numel() >= n)
+    rc = _lib.load().dk_argmax_finish(
+        argmax_keys.data_ptr(), n, tokens.data_ptr(), tokens_copy.data_ptr() if tokens_copy is not None else None,
+        lens_a.data_ptr() if lens_a is not None else None, lens_b.data_ptr() if lens_b is not None else None,
+        _lib.stream_ptr(tokens.device))
+    _lib.check(rc, "argmax_finish")
+    _lib.count_launch()
+    return tokens

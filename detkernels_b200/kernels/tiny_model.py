@@ -20,8 +20,10 @@ Drop-in for the reference's ``kernels/tiny_model.py``:
 kernel set on CUDA: a preallocated (zeroed) KV cache, prompts prefilled as
 rows through the same per-row kernels (attention row tiles give exactly the
 bits of token-by-token decoding), fused QKV and gate/up weights (every output
-column is computed exactly as by the separate matmul), and the decode step
-captured once in a CUDA graph and replayed.
+column is computed exactly as by the separate matmul), the element-wise ops
+fused into the matmul that produces their input (K/V written straight into the
+cache, residual adds, SiLU and SiLU*up, the greedy argmax) with the rounding of
+the unfused torch ops, and the decode step captured once in a CUDA graph.
 """
 from __future__ import annotations
 
@@ -29,7 +31,7 @@ from dataclasses import dataclass
 from typing import List, Optional, Sequence
 
 from .attention import attention_batch_invariant, attention_batch_variant, attention_decode, attention_reference
-from .matmul import matmul_batch_invariant, matmul_batch_variant, matmul_reference
+from .matmul import argmax_finish, matmul_batch_invariant, matmul_batch_variant, matmul_fused, matmul_reference
 from .rmsnorm import rmsnorm_batch_invariant, rmsnorm_batch_variant, rmsnorm_reference
 
 _KERNEL_SETS = {
@@ -123,6 +125,8 @@ class TinyModel:
 
     # ---- fused weights for the serving path (same bits per output column) ----
     def fused_layer_weights(self):
+        """Per layer: w_qkv = [w_q | w_k | w_v]; for SwiGLU, w_gu with gate and up columns
+        interleaved (2j = gate j, 2j+1 = up j) for the fused SiLU*up epilogue."""
         import torch
 
         fused = []
@@ -131,7 +135,8 @@ class TinyModel:
                  "w_mlp2": layer["w_mlp2"],
                  "w_qkv": torch.cat([layer["w_q"], layer["w_k"], layer["w_v"]], dim=1).contiguous()}
             if self.config.mlp == "swiglu":
-                f["w_gu"] = torch.cat([layer["w_gate"], layer["w_up"]], dim=1).contiguous()
+                f["w_gu"] = torch.stack([layer["w_gate"], layer["w_up"]], dim=2).reshape(
+                    layer["w_gate"].shape[0], -1).contiguous()
             else:
                 f["w_mlp1"] = layer["w_mlp1"]
             fused.append(f)
@@ -266,8 +271,9 @@ class DecodeEngine:
         self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
         # decode-step state
         self.tokens = torch.zeros(self.B, dtype=torch.long, device=dev)
-        self.kv_lens = torch.zeros(self.B, dtype=torch.int32, device=dev)
-        self.rows = torch.arange(self.B, device=dev)
+        self.kv_lens = torch.zeros(self.B, dtype=torch.int32, device=dev)   # cache write position
+        self.q_lens = torch.ones(self.B, dtype=torch.int32, device=dev)     # kv_lens + 1
+        self.argmax_keys = torch.zeros(self.B, dtype=torch.int64, device=dev)
         self._graphs = {}
         self._last_events = None
         # explicit scratch so captured graphs never allocate
@@ -283,41 +289,32 @@ class DecodeEngine:
         self.attn_ws = torch.zeros(max(a_ws, 1), dtype=torch.uint8, device=dev)
 
     # ---------------- building blocks (all per-row) ----------------
-    def _mm(self, x, w, ws=None):
-        return _matmul_ws(x, w, self.gemm_ws if ws is None else ws)
+    def _mm(self, x, w, epilogue="store", **kw):
+        return matmul_fused(x, w, epilogue, workspace=self.gemm_ws, **kw)
 
-    def _mlp(self, layer, xn):
-        import torch
-
-        F = self.cfg.mlp_hidden
-        if self.cfg.mlp == "swiglu":
-            gu = self._mm(xn, layer["w_gu"])
-            h = torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]
-        else:
-            h = torch.nn.functional.silu(self._mm(xn, layer["w_mlp1"]))
-        return self._mm(h, layer["w_mlp2"])
-
-    def _layer(self, li, layer, x, write_rows, write_pos, q_lens, row_tiles, max_len, attn_ws, events=None):
-        """One transformer block over R rows.  K/V of every row are written to
-        (write_rows, write_pos) before attention reads them."""
+    def _layer(self, li, layer, x, write_seq, write_pos, q_lens, row_tiles, max_len, attn_ws, events=None):
+        """One transformer block over R rows.  The QKV matmul writes K/V of every row
+        to (write_seq, write_pos) (int32; write_seq None: row r is sequence r) before
+        attention reads them."""
         cfg = self.cfg
         R = x.shape[0]
-        H, Hkv, D = self.H, self.Hkv, self.D
+        H, D = self.H, self.D
         xn = rmsnorm_batch_invariant(x, layer["norm1_w"], cfg.eps)
-        qkv = self._mm(xn, layer["w_qkv"])
-        q = qkv[:, :H * D].view(R, H, D)
-        k = qkv[:, H * D:(H + Hkv) * D].view(R, Hkv, D)
-        v = qkv[:, (H + Hkv) * D:].view(R, Hkv, D)
-        self.k_cache[li][write_rows, :, write_pos, :] = k
-        self.v_cache[li][write_rows, :, write_pos, :] = v
+        q = self._mm(xn, layer["w_qkv"], "qkv_cache", q_cols=H * D, head_dim=D, k_cache=self.k_cache[li],
+                     v_cache=self.v_cache[li], row_seq=write_seq, row_pos=write_pos)
         if events is not None:
             events[0].record()
-        attn = attention_decode(q, self.k_cache[li], self.v_cache[li], q_lens, row_tiles=row_tiles,
+        attn = attention_decode(q.view(R, H, D), self.k_cache[li], self.v_cache[li], q_lens, row_tiles=row_tiles,
                                 max_kv_len=max_len, workspace=attn_ws)
         if events is not None:
             events[1].record()
-        x = x + self._mm(attn.reshape(R, H * D), layer["w_o"])
-        return x + self._mlp(layer, rmsnorm_batch_invariant(x, layer["norm2_w"], cfg.eps))
+        x = self._mm(attn.reshape(R, H * D), layer["w_o"], "residual", residual=x)
+        xn = rmsnorm_batch_invariant(x, layer["norm2_w"], cfg.eps)
+        if cfg.mlp == "swiglu":
+            hid = self._mm(xn, layer["w_gu"], "silu_mul")
+        else:
+            hid = self._mm(xn, layer["w_mlp1"], "silu")
+        return self._mm(hid, layer["w_mlp2"], "residual", residual=x)
 
     def _logits(self, x):
         xn = rmsnorm_batch_invariant(x, self.model.norm_f_w, self.cfg.eps)
@@ -352,6 +349,8 @@ class DecodeEngine:
         }
         plan = {k: v.pin_memory().to(dev, non_blocking=True) for k, v in host.items()}
         plan["q_lens"] = (plan["pos"] + 1).to(torch.int32)
+        plan["rows32"] = plan["rows"].to(torch.int32)
+        plan["pos32"] = plan["pos"].to(torch.int32)
         plan["B"] = B
         plan["max_len"] = max(len(p) for p in prompts)
         plan["h2d_bytes"] = sum(v.numel() * v.element_size() for v in host.values())
@@ -373,36 +372,35 @@ class DecodeEngine:
         try:
             x = self.model.embed[plan["tok"]]
             for li, layer in enumerate(self.layers):
-                x = self._layer(li, layer, x, plan["rows"], plan["pos"], plan["q_lens"], plan["tiles"],
+                x = self._layer(li, layer, x, plan["rows32"], plan["pos32"], plan["q_lens"], plan["tiles"],
                                 plan["max_len"], plan["attn_ws"])
             logits = self._logits(x[plan["last"]])
         finally:
             self.gemm_ws = saved
         self.kv_lens.zero_()
         self.kv_lens[:plan["B"]] = plan["lens"]
+        self.q_lens.copy_(self.kv_lens + 1)
         return logits
 
     # ---------------- decode ----------------
-    def _decode_step(self, max_len, events=None):
-        """tokens -> next tokens for all rows; K/V written at kv_lens, then kv_lens += 1.
-        max_len bounds every row's length after this step (sizes the attention grid)."""
+    def _decode_step(self, max_len, out_row=None, events=None):
+        """tokens -> next tokens (also into out_row) for all rows; K/V written at kv_lens,
+        then kv_lens and q_lens advance.  max_len bounds every row's length after this
+        step (sizes the attention grid)."""
         import torch
 
         x = self.model.embed[self.tokens]
-        pos = self.kv_lens.long()
-        q_lens = self.kv_lens + 1
         for li, layer in enumerate(self.layers):
+            ev = None
             if events is not None:
                 ev = (torch.cuda.Event(enable_timing=True, external=True),
                       torch.cuda.Event(enable_timing=True, external=True))
                 events.append(ev)
-                x = self._layer(li, layer, x, self.rows, pos, q_lens, None, max_len, self.attn_ws, ev)
-            else:
-                x = self._layer(li, layer, x, self.rows, pos, q_lens, None, max_len, self.attn_ws)
-        nxt = self._logits(x).argmax(dim=-1)
-        self.tokens.copy_(nxt)
-        self.kv_lens.add_(1)
-        return nxt
+            x = self._layer(li, layer, x, None, self.kv_lens, self.q_lens, None, max_len, self.attn_ws, ev)
+        xn = rmsnorm_batch_invariant(x, self.model.norm_f_w, self.cfg.eps)
+        self._mm(xn, self.model.w_lm_head, "argmax", argmax_keys=self.argmax_keys)
+        argmax_finish(self.argmax_keys, self.tokens, out_row, self.kv_lens, self.q_lens)
+        return self.tokens
 
     def _capture(self, n_steps, start_len, timing):
         """Capture n_steps decode steps (one graph) starting from rows of length <= start_len."""
@@ -411,18 +409,19 @@ class DecodeEngine:
         out = torch.empty((n_steps, self.B), dtype=torch.long, device=self.device)
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
-        saved = (self.tokens.clone(), self.kv_lens.clone())
+        saved = (self.tokens.clone(), self.kv_lens.clone(), self.q_lens.clone())
         with torch.cuda.stream(s):   # warm-up: lazy loads and tensor-map encoding
             self._decode_step(start_len + 1)
         torch.cuda.current_stream(self.device).wait_stream(s)
         self.tokens.copy_(saved[0])
         self.kv_lens.copy_(saved[1])
+        self.q_lens.copy_(saved[2])
         events = [] if timing else None
         g = torch.cuda.CUDAGraph()
         n0 = self._lib.launch_count()
         with torch.cuda.graph(g):
             for t in range(n_steps):
-                out[t].copy_(self._decode_step(min(start_len + t + 1, self.S), events))
+                self._decode_step(min(start_len + t + 1, self.S), out[t], events)
         n_graph = self._lib.launch_count() - n0
         self._lib.count_launch(-n_graph)  # recorded, not executed; counted at each replay
         return g, out, events, n_graph
@@ -441,7 +440,7 @@ class DecodeEngine:
         if not self.use_graph:
             out = torch.empty((n_steps, self.B), dtype=torch.long, device=self.device)
             for t in range(n_steps):
-                out[t].copy_(self._decode_step(min(start_len + t + 1, self.S)))
+                self._decode_step(min(start_len + t + 1, self.S), out[t])
             return out
         key = (n_steps, start_len, timing)
         if key not in self._graphs:
@@ -483,23 +482,3 @@ class DecodeEngine:
     def generate(self, prompts: Sequence[Sequence[int]], n_steps: int):
         """Greedy decode of n_steps tokens after each prompt; returns [B, n_steps] (device)."""
         return self.run(self.plan(prompts), n_steps)
-
-
-def _matmul_ws(x, w, ws):
-    """matmul_batch_invariant with a caller-owned workspace (no allocation, graph-safe)."""
-    import torch
-
-    from detkernels_b200 import _lib
-    from .matmul import _tma_ready
-
-    M, K = x.shape
-    N = w.shape[1]
-    c = torch.empty((M, N), device=x.device, dtype=x.dtype)
-    a = _tma_ready(x)
-    lib = _lib.load()
-    rc = lib.dk_matmul_batch_invariant(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), c.data_ptr(),
-                                       c.stride(0), M, N, K, _lib.dtype_code(x.dtype), ws.data_ptr(), ws.numel(),
-                                       _lib.stream_ptr(x.device))
-    _lib.check(rc, "matmul_batch_invariant")
-    _lib.count_launch()
-    return c

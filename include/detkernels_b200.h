@@ -122,6 +122,49 @@ int dk_matmul_batch_variant(const void* a, int64_t lda, const void* b, int64_t l
                             int64_t M, int64_t N, int64_t K, int dtype, int split_m_threshold, int split_k,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- Matmul with a fused epilogue ----
+ * What happens to each output element's f32 tree sum v(m, n) before it is stored.  Every step rounds
+ * exactly where the unfused torch ops of a decoder block round (matmul output, residual add, SiLU,
+ * product), so a fused call returns the bits of the unfused sequence. */
+#define DK_EPI_STORE 0     /* C[m,n] = round(v) */
+#define DK_EPI_RESIDUAL 1  /* C[m,n] = round(R[m,n] + round(v)); R may be C itself */
+#define DK_EPI_SILU 2      /* C[m,n] = round(silu(round(v))), silu(x) = x / (1 + exp(-x)) */
+#define DK_EPI_SILU_MUL 3  /* B's columns hold gate/up pairs (2j, 2j+1); C is [M, N/2]:
+                              C[m,j] = round(round(silu(round(v(m,2j)))) * round(v(m,2j+1))) */
+#define DK_EPI_QKV_CACHE 4 /* columns [0, q_cols) -> C[m, n]; the next kv_cols -> K cache, the next kv_cols ->
+                              V cache, at (row_seq[m], n' / head_dim, row_pos[m], n' % head_dim) */
+#define DK_EPI_ARGMAX 5    /* per row, the first column holding the largest round(v) (NaN above all, -0 == +0),
+                              torch.argmax's answer, folded into argmax_keys[m] with 64-bit atomicMax of
+                              (ordered value << 32 | ~n): order-free, so deterministic.  C is optional
+                              (NULL: logits are not stored).  argmax_keys must be 0 before the call;
+                              dk_argmax_finish reads and re-zeroes them. */
+typedef struct dk_matmul_epilogue {
+  int mode;
+  const void* resid;       /* DK_EPI_RESIDUAL: R, same dtype as C */
+  int64_t ld_resid;
+  int32_t q_cols, kv_cols, head_dim;  /* DK_EPI_QKV_CACHE */
+  void* k_cache;
+  void* v_cache;
+  int64_t cache_stride_seq, cache_stride_head, cache_stride_tok;  /* elements; unit stride along d */
+  const int32_t* row_seq;  /* device int32[M]; NULL: row m writes cache sequence m */
+  const int32_t* row_pos;  /* device int32[M]: token position written by row m */
+  unsigned long long* argmax_keys;  /* DK_EPI_ARGMAX: device uint64[M] */
+} dk_matmul_epilogue;
+
+/* dk_matmul_batch_invariant followed by the epilogue `epi` (same K numerics; NULL epi = DK_EPI_STORE).
+ * No counterpart in the reference: it fuses the reference decoder's element-wise torch ops
+ * (tiny_model.py:110-139) into the matmul that produces their input. */
+int dk_matmul_batch_invariant_ex(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+                                 int64_t M, int64_t N, int64_t K, int dtype, const dk_matmul_epilogue* epi,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* End of a greedy decode step after a DK_EPI_ARGMAX matmul, one thread per row: tokens[r] = the row's
+ * argmax column (also into tokens_copy[r] when non-NULL), keys[r] = 0, and lens_a[r] += 1,
+ * lens_b[r] += 1 for the non-NULL ones.  No counterpart in the reference: it replaces the
+ * `logits.argmax(-1)` and cache-length bookkeeping of tiny_model.py:150-157. */
+int dk_argmax_finish(unsigned long long* keys, int64_t n_rows, int64_t* tokens, int64_t* tokens_copy,
+                     int32_t* lens_a, int32_t* lens_b, void* stream);
+
 /* ---- Decode attention (one query per row, split-KV with a fixed split size) ----
  * q:   [n_rows, n_q_heads, head_dim], strides (q_stride_row, q_stride_head), unit d stride.
  * k,v: KV cache viewed as [kv_n_seq, n_kv_heads, kv_capacity, head_dim] with element strides
