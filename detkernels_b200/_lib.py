@@ -53,6 +53,9 @@ SIGNATURES = {
                                          _c_void_p, _size, _c_void_p]),
     "dk_matmul_batch_invariant_ex": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _i64,
                                             _int, _c_void_p, _c_void_p, _size, _c_void_p]),
+    "dk_gdn_forward": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
+                              _int, _int, _int, _int, _int, _int, ctypes.c_float, _c_void_p, _int, _c_void_p, _int,
+                              _c_void_p]),
     "dk_argmax_finish": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "dk_matmul_slice_partials": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _int, _int,
                                         _int, _c_void_p]),

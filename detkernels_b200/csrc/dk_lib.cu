@@ -16,6 +16,7 @@
 #include "dk_gemm.cuh"
 #include "dk_attention.cuh"
 #include "dk_attention_variant.cuh"
+#include "dk_gdn.cuh"
 
 namespace {
 
@@ -398,6 +399,26 @@ int attn_launch(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Pa
   constexpr int kNarrow = (4 < dk::attn::Cfg<D>::KMAX) ? 4 : dk::attn::Cfg<D>::KMAX;
   if (p.rows_cap * D <= kNarrow * kThr) return attn_launch_km<T, D, kNarrow>(tk, tv, p, grid_x, grid_y, st);
   return attn_launch_km<T, D, dk::attn::Cfg<D>::KMAX>(tk, tv, p, grid_x, grid_y, st);
+}
+
+template <typename T, int DK, int DV>
+int gdn_launch_t(const dk::gdn::Params& p, int64_t n_seqs, cudaStream_t st) {
+  static bool done[kMaxDevices] = {};
+  auto fn = dk::gdn::gdn_chunk_kernel<T, DK, DV>;
+  const int bytes = static_cast<int>(dk::gdn::Smem<DK, DV>::kBytes);
+  int rc = ensure_smem(fn, bytes, done);
+  if (rc) return rc;
+  cudaError_t e = launch_pdl(fn, dim3(p.HV, static_cast<unsigned>(n_seqs)), dim3(dk::gdn::kThreads), bytes, st, p);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "gdn: launch failed: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
+
+template <typename T>
+int gdn_launch_dims(const dk::gdn::Params& p, int dk_, int dv_, int64_t n_seqs, cudaStream_t st) {
+  if (dk_ == 128 && dv_ == 128) return gdn_launch_t<T, 128, 128>(p, n_seqs, st);
+  if (dk_ == 64 && dv_ == 64) return gdn_launch_t<T, 64, 64>(p, n_seqs, st);
+  if (dk_ == 32 && dv_ == 32) return gdn_launch_t<T, 32, 32>(p, n_seqs, st);
+  return fail(DK_ERR_UNSUPPORTED, "gdn: head dims (%d, %d) not built (32/32, 64/64, 128/128)", dk_, dv_);
 }
 
 }  // namespace
@@ -924,3 +945,42 @@ int dk_attention_batch_invariant_noalloc(const void* q, int64_t q_stride_row, in
 }
 
 }  // extern "C"
+
+int dk_gdn_forward(const void* q, const void* k, const void* v, const void* g, const void* beta, void* o,
+                   const int64_t* cu_seqlens, int64_t n_seqs, int64_t seq_len, int n_heads, int n_v_heads,
+                   int head_dim_k, int head_dim_v, int dtype, int gb_dtype, float scale, const void* initial_state,
+                   int state_dtype, float* final_state, int chunk_size, void* stream) {
+  const char* what = "gdn_forward";
+  if (dtype != DK_BF16 && dtype != DK_F16) return fail(DK_ERR_UNSUPPORTED, "%s: q/k/v must be bf16 or f16", what);
+  auto ok_dt = [](int d) { return d == DK_F32 || d == DK_BF16 || d == DK_F16; };
+  if (!ok_dt(gb_dtype) || (initial_state && !ok_dt(state_dtype)))
+    return fail(DK_ERR_UNSUPPORTED, "%s: g/beta and the initial state must be f32, bf16 or f16", what);
+  if (n_seqs < 0 || seq_len < 0 || n_heads <= 0 || n_v_heads <= 0 || n_v_heads % n_heads)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad sizes (n_v_heads must be a multiple of n_heads)", what);
+  if (chunk_size != 1 && chunk_size != dk::gdn::kChunk)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: chunk_size must be 1 or %d", what, dk::gdn::kChunk);
+  if (n_seqs > 65535 || n_v_heads > 65535) return fail(DK_ERR_UNSUPPORTED, "%s: too many sequences or heads", what);
+  if (!(scale == scale)) return fail(DK_ERR_INVALID_ARGUMENT, "%s: scale is NaN", what);
+  if (n_seqs == 0) return DK_OK;
+  if (!q || !k || !v || !g || !beta || !o) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null tensor", what);
+  dk::gdn::Params p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.g = g;
+  p.beta = beta;
+  p.o = o;
+  p.cu_seqlens = cu_seqlens;
+  p.seq_len = seq_len;
+  p.h0 = initial_state;
+  p.ht = final_state;
+  p.H = n_heads;
+  p.HV = n_v_heads;
+  p.gb_dtype = gb_dtype;
+  p.h0_dtype = state_dtype;
+  p.chunk = chunk_size;
+  p.scale = scale;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == DK_BF16) return gdn_launch_dims<__nv_bfloat16>(p, head_dim_k, head_dim_v, n_seqs, st);
+  return gdn_launch_dims<__half>(p, head_dim_k, head_dim_v, n_seqs, st);
+}

@@ -225,6 +225,21 @@ int dk_attention_batch_invariant_noalloc(const void* q, int64_t q_stride_row, in
                                          int32_t n_rows, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
                                          int32_t max_kv_len, float scale, int dtype, void* stream);
 
+/* ---- Gated delta rule (Gated DeltaNet linear attention), forward ----
+ * replaces the FLA `chunk_gated_delta_rule` / `fused_recurrent_gated_delta_rule` calls of the
+ * reference's gdn/repro.py:76,161-162,293-294 (fla 0.5.1 API, [B, T, heads, dim] layout).
+ * q, k: [tokens, n_heads, head_dim_k]; v: [tokens, n_v_heads, head_dim_v]; g (log decay), beta:
+ * [tokens, n_v_heads]; o: [tokens, n_v_heads, head_dim_v] in q's dtype, all contiguous.  Value head j
+ * uses query/key head j / (n_v_heads / n_heads).  Sequences: cu_seqlens (device int64[n_seqs + 1])
+ * or, when NULL, n_seqs rows of seq_len tokens each.  initial_state / final_state: [n_seqs,
+ * n_v_heads, head_dim_k, head_dim_v] (final in f32), either may be NULL.  chunk_size 64 computes
+ * 64-token chunks from each sequence's start (chunked form); 1 steps token by token.  A sequence's
+ * result never depends on the other sequences of the call.  Head dims: 32/32, 64/64, 128/128. */
+int dk_gdn_forward(const void* q, const void* k, const void* v, const void* g, const void* beta, void* o,
+                   const int64_t* cu_seqlens, int64_t n_seqs, int64_t seq_len, int n_heads, int n_v_heads,
+                   int head_dim_k, int head_dim_v, int dtype, int gb_dtype, float scale, const void* initial_state,
+                   int state_dtype, float* final_state, int chunk_size, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
