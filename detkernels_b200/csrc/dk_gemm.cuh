@@ -102,6 +102,8 @@ enum Mode : int { FOLD = 0, SPLIT = 1, PARTIAL = 2, ATOMIC = 3 };
 struct Params {
   dk_matmul_epilogue epi;        // what is done with each final value (DK_EPI_*)
   int M, N, K;
+  int k_base;      // global K index of the first column of A / row of B held in memory (K shards)
+  int k_extent;    // K columns of A / rows of B held in memory (0: K)
   int slice_len;                 // elements per slice (multiple of 16)
   int slice_begin, slice_end;    // slices computed by this launch
   int group;                     // slices per work unit (aligned group, power of two)
@@ -338,9 +340,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t* st = smem + stage * stage_bytes;
             mbar_arrive_expect_tx(&full[stage], tx_bytes);
             const int kk = k0 + kb * kBK;
-            tma_load_2d(st, &tmB, &full[stage], nt * kTileN, kk);
-            tma_load_2d(st + kWBoxBytes, &tmB, &full[stage], nt * kTileN + 64, kk);
-            tma_load_2d(st + kWTileBytes, &tmA, &full[stage], kk, mt * kTileM);
+            const int kl = kk - p.k_base;   // coordinate inside the K range held in memory
+            tma_load_2d(st, &tmB, &full[stage], nt * kTileN, kl);
+            tma_load_2d(st + kWBoxBytes, &tmB, &full[stage], nt * kTileN + 64, kl);
+            tma_load_2d(st + kWTileBytes, &tmA, &full[stage], kl, mt * kTileM);
             ++fills;
             if (++stage == n_stages) {
               stage = 0;

@@ -289,11 +289,12 @@ int launch_fold(const float* partials, int n_parts, const dk::gemm::Params& p, c
 int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb, dk::gemm::Params p,
                 cudaStream_t st, const char* what) {
   p.a_rows = (p.m_tiles == 1) ? static_cast<int>(ceil_div(p.M, 8) * 8) : dk::gemm::kTileM;
+  const int64_t k_mem = p.k_extent > 0 ? p.k_extent : p.K;
   CUtensorMap tmB, tmA;
-  const uint64_t dimsB[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.K)};
+  const uint64_t dimsB[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(k_mem)};
   const uint64_t strB[1] = {static_cast<uint64_t>(ldb) * 2};
   const uint32_t boxB[2] = {64, static_cast<uint32_t>(dk::gemm::kBK)};
-  const uint64_t dimsA[2] = {static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M)};
+  const uint64_t dimsA[2] = {static_cast<uint64_t>(k_mem), static_cast<uint64_t>(p.M)};
   const uint64_t strA[1] = {static_cast<uint64_t>(lda) * 2};
   const uint32_t boxA[2] = {static_cast<uint32_t>(dk::gemm::kBK), static_cast<uint32_t>(p.a_rows)};
   const CUtensorMapDataType dt = (dtype == DK_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -670,6 +671,57 @@ int dk_matmul_slice_partials(const void* a, int64_t lda, const void* b, int64_t 
   p.mode = dk::gemm::PARTIAL;
   p.ws = partials;
   return gemm_launch(dtype, a, lda, b, ldb, p, st, what);
+}
+
+int dk_matmul_shard_partials(const void* a, int64_t lda, const void* b, int64_t ldb, float* partial, int64_t M,
+                             int64_t N, int64_t K, int slice_begin, int slice_end, int dtype, void* stream) {
+  const char* what = "matmul_shard_partials";
+  const int span = slice_end - slice_begin;
+  if (slice_begin < 0 || slice_end > dk::gemm::kSlices || span <= 0 || (span & (span - 1)) != 0 ||
+      slice_begin % span != 0)
+    return fail(DK_ERR_INVALID_ARGUMENT,
+                "%s: slice range [%d, %d) is not an aligned group of 1, 2, 4 or 8 slices", what, slice_begin,
+                slice_end);
+  if (K < 0 || K > 0x7fffffffLL) return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad K", what);
+  int64_t k0, k1;
+  dk_matmul_shard_range(K, slice_begin, slice_end, &k0, &k1);
+  const int64_t k_loc = k1 - k0;
+  if (k_loc == 0) {
+    if (M == 0 || N == 0) return DK_OK;
+    if (!partial) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null partial", what);
+    cudaError_t e = cudaMemsetAsync(partial, 0, sizeof(float) * M * N, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? DK_OK : fail(DK_ERR_CUDA, "%s: memset: %s", what, cudaGetErrorString(e));
+  }
+  int rc = gemm_validate(a, lda, b, ldb, M, N, k_loc, dtype, what);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return DK_OK;
+  if (!partial) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null partial", what);
+  dk::gemm::Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.k_base = static_cast<int>(k0);
+  p.k_extent = static_cast<int>(k_loc);
+  p.slice_len = slice_len_for(K, dk::gemm::kSlices);
+  p.slice_begin = slice_begin;
+  p.slice_end = slice_end;
+  p.group = span;
+  p.n_tiles = static_cast<int>(ceil_div(N, dk::gemm::kTileN));
+  p.m_tiles = static_cast<int>(ceil_div(M, dk::gemm::kTileM));
+  p.mode = dk::gemm::PARTIAL;
+  p.ws = partial;
+  return gemm_launch(dtype, a, lda, b, ldb, p, static_cast<cudaStream_t>(stream), what);
+}
+
+void dk_matmul_shard_range(int64_t K, int slice_begin, int slice_end, int64_t* k_begin, int64_t* k_end) {
+  const int64_t L = (K <= 0) ? 0 : slice_len_for(K, dk::gemm::kSlices);
+  int64_t b = L * slice_begin, e = L * slice_end;
+  if (b > K) b = K;
+  if (e > K) e = K;
+  if (b < 0) b = 0;
+  if (e < b) e = b;
+  if (k_begin) *k_begin = b;
+  if (k_end) *k_end = e;
 }
 
 int dk_matmul_fold_slices(const float* partials, int n_parts, void* c, int64_t ldc, int64_t M, int64_t N, int dtype,

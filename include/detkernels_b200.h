@@ -109,6 +109,15 @@ int dk_matmul_batch_invariant(const void* a, int64_t lda, const void* b, int64_t
 int dk_matmul_slice_partials(const void* a, int64_t lda, const void* b, int64_t ldb, float* partial,
                              int64_t M, int64_t N, int64_t K, int slice_begin, int slice_end, int dtype,
                              void* stream);
+/* Row-parallel tensor parallelism on K shards.  dk_matmul_shard_range gives the K range [k_begin,
+ * k_end) of the full K that an aligned slice group [slice_begin, slice_end) covers; a rank holding only
+ * that range -- a: [M, k_end - k_begin] (its columns of A), b: [k_end - k_begin, N] (its rows of B) --
+ * calls dk_matmul_shard_partials with the FULL K to get the group's f32 subtree sum, bit-identical to
+ * dk_matmul_slice_partials on the unsharded operands.  No counterpart in the reference (its matmul has
+ * no tensor parallelism, kernels/matmul.py:161-186). */
+void dk_matmul_shard_range(int64_t K, int slice_begin, int slice_end, int64_t* k_begin, int64_t* k_end);
+int dk_matmul_shard_partials(const void* a, int64_t lda, const void* b, int64_t ldb, float* partial, int64_t M,
+                             int64_t N, int64_t K, int slice_begin, int slice_end, int dtype, void* stream);
 /* out[m,n] = the upper tree levels over n_parts (1, 2, 4 or 8) subtree sums in group order,
  * partials[j * M * N + m * N + n], rounded to dtype: reproduces dk_matmul_batch_invariant bit for bit. */
 int dk_matmul_fold_slices(const float* partials, int n_parts, void* c, int64_t ldc, int64_t M, int64_t N,

@@ -32,6 +32,35 @@ def matmul(a, b, dtype="bfloat16"):
     return round_to(a32 @ b32, dtype)
 
 
+def slice_len(K, n_slices=8):
+    """Slice length of the batch-invariant matmul's K split: ceil16(ceil(K / 8))."""
+    per = -(-K // n_slices)
+    return -(-per // 16) * 16
+
+
+def matmul_slice_partials(a, b, slice_begin=0, slice_end=8):
+    """f32 partial products of K slices [slice_begin, slice_end) of a @ b, each [M, N]
+    (the split that detkernels_b200's invariant matmul folds; tolerance oracle for its
+    per-slice sums, exact bookkeeping oracle for sharding and fold order)."""
+    a32 = np.asarray(a, dtype=np.float32)
+    b32 = np.asarray(b, dtype=np.float32)
+    K = a32.shape[1]
+    L = slice_len(K)
+    out = []
+    for s in range(slice_begin, slice_end):
+        k0, k1 = min(s * L, K), min((s + 1) * L, K)
+        out.append(a32[:, k0:k1] @ b32[k0:k1] if k1 > k0 else np.zeros((a32.shape[0], b32.shape[1]), np.float32))
+    return out
+
+
+def fold_tree(parts):
+    """Pairwise tree over 1, 2, 4 or 8 f32 partials in order: ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7))."""
+    parts = [np.asarray(p, dtype=np.float32) for p in parts]
+    while len(parts) > 1:
+        parts = [(parts[i] + parts[i + 1]).astype(np.float32) for i in range(0, len(parts), 2)]
+    return parts[0]
+
+
 def matmul_f64(a, b):
     """Exact-ish f64 product of the operand values (for error bounds)."""
     return np.asarray(a, dtype=np.float64) @ np.asarray(b, dtype=np.float64)
