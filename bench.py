@@ -241,6 +241,90 @@ def gemm_vs_cublas(iters=10):
     return res
 
 
+# ----------------------------------------------------------------------------- gated delta rule
+GDN = dict(n_seqs=64, min_len=256, max_len=4096, H=16, HV=32, D=128, decode_steps=300)
+
+
+def gdn_bench(peaks, iters=3):
+    """Chunked prefill of 64 packed sequences (lengths U{256..4096}) and 300 single-token
+    decode steps of the same 64 sequences, GVA 16 q/k heads / 32 v heads, d = 128, bf16
+    inputs, f32 state.  Inputs exceed L2 (prefill q/k/v ~2 GB, decode state 134 MB x 2)."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+
+    from detkernels_b200.kernels.gdn import chunk_gated_delta_rule, fused_recurrent_gated_delta_rule
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = GDN
+    rng = np.random.default_rng(7)
+    lens = rng.integers(cfg["min_len"], cfg["max_len"] + 1, cfg["n_seqs"])
+    T = int(lens.sum())
+    H, HV, D = cfg["H"], cfg["HV"], cfg["D"]
+    g = torch.Generator(device=dev).manual_seed(7)
+    q = torch.randn(1, T, H, D, device=dev, generator=g).to(torch.bfloat16)
+    k = F.normalize(torch.randn(1, T, H, D, device=dev, generator=g), p=2, dim=-1).to(torch.bfloat16)
+    v = torch.randn(1, T, HV, D, device=dev, generator=g).to(torch.bfloat16)
+    gate = F.logsigmoid(torch.randn(1, T, HV, device=dev, generator=g)).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(1, T, HV, device=dev, generator=g)).to(torch.bfloat16)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), device=dev, dtype=torch.long)
+
+    def timed(fn, n):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(n):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            ts.append(s.elapsed_time(e))
+        return statistics.median(ts)
+
+    state = {}
+
+    def prefill():
+        state["o"], state["h"] = chunk_gated_delta_rule(q, k, v, gate, beta, output_final_state=True, cu_seqlens=cu)
+
+    t_pre = timed(prefill, iters)
+    # algorithmic work of the chunked form (per v-head, 64-token chunk, d = 128)
+    bytes_tok = (H * D * 2) * 2 + (HV * D * 2) * 2 + HV * 2 * 2
+    flops_chunk = 6 * 64 * D * D + 10 * 64 * 64 * D + (2 / 3) * 64 ** 3
+    pre_bytes = bytes_tok * T + cfg["n_seqs"] * HV * D * D * 4
+    pre_flops = flops_chunk * HV * T / 64
+
+    n = cfg["n_seqs"]
+    steps = cfg["decode_steps"]
+    dq = torch.randn(steps, n, 1, H, D, device=dev, generator=g).to(torch.bfloat16)
+    dk = F.normalize(torch.randn(steps, n, 1, H, D, device=dev, generator=g), p=2, dim=-1).to(torch.bfloat16)
+    dv = torch.randn(steps, n, 1, HV, D, device=dev, generator=g).to(torch.bfloat16)
+    dg = F.logsigmoid(torch.randn(steps, n, 1, HV, device=dev, generator=g)).to(torch.bfloat16)
+    db = torch.sigmoid(torch.randn(steps, n, 1, HV, device=dev, generator=g)).to(torch.bfloat16)
+
+    def decode():
+        h = state["h"]
+        for t in range(steps):
+            _, h = fused_recurrent_gated_delta_rule(dq[t], dk[t], dv[t], dg[t], db[t], initial_state=h,
+                                                    output_final_state=True)
+
+    t_dec = timed(decode, 1)
+    dec_bytes = steps * (2 * n * HV * D * D * 4 + n * ((H * D * 2) * 2 + (HV * D * 2) * 2 + HV * 4))
+    hbm = peaks["hbm_gbs"]
+    return {
+        "workload": "GDN: %d seqs x U{%d..%d} tok (T=%d), H %d / HV %d, d %d, bf16, f32 state; then %d decode steps"
+                    % (n, cfg["min_len"], cfg["max_len"], T, H, HV, D, steps),
+        "prefill": {"tok_per_s": round(T / t_pre * 1e3, 1), "ms": round(t_pre, 3),
+                    "achieved_gbs": round(pre_bytes / t_pre / 1e6, 1),
+                    "frac_hbm": round(pre_bytes / t_pre / 1e6 / hbm, 4),
+                    "achieved_tflops": round(pre_flops / t_pre / 1e9, 2),
+                    "frac_bf16_peak": round(pre_flops / t_pre / 1e9 / peaks["bf16_tflops"], 4)},
+        "decode": {"steps_per_s": round(steps / t_dec * 1e3, 1), "us_per_step": round(t_dec / steps * 1e3, 2),
+                   "achieved_gbs": round(dec_bytes / t_dec / 1e6, 1),
+                   "frac_hbm": round(dec_bytes / t_dec / 1e6 / hbm, 4)},
+    }
+
+
 # ----------------------------------------------------------------------------- main arms
 def run_reference(args, rank, world):
     """CPU path of the reference algorithm (numpy oracle), rank 0 only."""
@@ -385,6 +469,7 @@ def run_ours(args, rank, world, local):
                   "tracked_prefix_match": int(np.argmin(np.append(ours_small[0] == cpu_toks[0], False)))}
 
     gemm = gemm_vs_cublas() if not args.skip_gemm else None
+    gdn = gdn_bench(peaks) if not args.skip_gdn and rank == 0 else None
 
     line = {
         "metric": "BI decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
@@ -404,6 +489,7 @@ def run_ours(args, rank, world, local):
         "divergences": divergences,
         "parity": parity,
         "gemm_vs_cublas": gemm,
+        "gdn": gdn,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -419,6 +505,7 @@ def main(argv=None):
     ap.add_argument("--skip-gemm", action="store_true", help="skip the GEMM-vs-cuBLAS table")
     ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the end-to-end public-API timing")
+    ap.add_argument("--skip-gdn", action="store_true", help="skip the gated-delta-rule section")
     ap.add_argument("--new-tokens", type=int, default=NEW_TOKENS,
                     help="tokens generated per prompt (the workload is 128; smaller only for profiling)")
     args = ap.parse_args(argv)
