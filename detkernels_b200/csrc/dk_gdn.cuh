@@ -276,5 +276,91 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Params p) 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Token-by-token recurrence (decode; fused_recurrent_gated_delta_rule), in the
+// order of the published recurrence: S <- exp(g) S; u = S^T k; v' = beta (v - u);
+// S <- S + k v'^T; o = S^T (scale q).  One CTA per (value head, sequence, block of
+// 32 value columns); warp w holds rows [w DK/4, (w+1) DK/4) of those columns in
+// registers (lane = column), so the state is read and written exactly once per
+// call.  Sums over rows: each warp's rows in ascending order, then the four warp
+// partials ((w0 + w1) + w2) + w3.
+// ---------------------------------------------------------------------------
+constexpr int kRecWarps = 4;
+
+template <typename T, int DK, int DV>
+__global__ void __launch_bounds__(32 * kRecWarps) gdn_recurrent_kernel(const Params p) {
+  constexpr int kRows = DK / kRecWarps;
+  __shared__ float kk[DK], qq[DK];
+  __shared__ float red[2][kRecWarps][32];
+  __shared__ float sc[2];
+  pdl_wait();
+  const int hv = blockIdx.x;
+  const int n = blockIdx.y;
+  const int HV = p.HV;
+  const int hq = hv / (HV / p.H);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.z * 32 + lane;
+  const int row0 = warp * kRows;
+  int64_t bos, len;
+  if (p.cu_seqlens) {
+    bos = p.cu_seqlens[n];
+    len = p.cu_seqlens[n + 1] - bos;
+  } else {
+    bos = static_cast<int64_t>(n) * p.seq_len;
+    len = p.seq_len;
+  }
+  const T* q = static_cast<const T*>(p.q);
+  const T* k = static_cast<const T*>(p.k);
+  const T* v = static_cast<const T*>(p.v);
+  T* o = static_cast<T*>(p.o);
+  const int64_t sbase = (static_cast<int64_t>(n) * HV + hv) * DK * DV;
+  float s[kRows];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r)
+    s[r] = p.h0 ? load_any(p.h0, sbase + static_cast<int64_t>(row0 + r) * DV + c, p.h0_dtype) : 0.0f;
+
+  for (int64_t t = 0; t < len; ++t) {
+    const int64_t tok = bos + t;
+    __syncthreads();  // the previous token is done with kk, qq, red, sc
+    for (int i = threadIdx.x; i < DK; i += 32 * kRecWarps) {
+      const int64_t off = (tok * p.H + hq) * DK + i;
+      kk[i] = to_f32<T>(k[off]);
+      qq[i] = __fmul_rn(to_f32<T>(q[off]), p.scale);
+    }
+    if (threadIdx.x == 0) {
+      sc[0] = expf(load_any(p.g, tok * HV + hv, p.gb_dtype));
+      sc[1] = load_any(p.beta, tok * HV + hv, p.gb_dtype);
+    }
+    __syncthreads();
+    const float e = sc[0], b = sc[1];
+    float u = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      s[r] = __fmul_rn(s[r], e);
+      u = __fmaf_rn(s[r], kk[row0 + r], u);
+    }
+    red[0][warp][lane] = u;
+    __syncthreads();
+    const float us = __fadd_rn(__fadd_rn(__fadd_rn(red[0][0][lane], red[0][1][lane]), red[0][2][lane]), red[0][3][lane]);
+    const float vp = __fmul_rn(b, __fsub_rn(to_f32<T>(v[(tok * HV + hv) * DV + c]), us));
+    float ov = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      s[r] = __fmaf_rn(kk[row0 + r], vp, s[r]);
+      ov = __fmaf_rn(s[r], qq[row0 + r], ov);
+    }
+    red[1][warp][lane] = ov;
+    __syncthreads();
+    if (warp == 0) {
+      const float os = __fadd_rn(__fadd_rn(__fadd_rn(red[1][0][lane], red[1][1][lane]), red[1][2][lane]), red[1][3][lane]);
+      o[(tok * HV + hv) * DV + c] = from_f32<T>(os);
+    }
+  }
+  if (p.ht) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) p.ht[sbase + static_cast<int64_t>(row0 + r) * DV + c] = s[r];
+  }
+}
+
 }  // namespace gdn
 }  // namespace dk

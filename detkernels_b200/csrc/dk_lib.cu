@@ -404,6 +404,13 @@ int attn_launch(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Pa
 
 template <typename T, int DK, int DV>
 int gdn_launch_t(const dk::gdn::Params& p, int64_t n_seqs, cudaStream_t st) {
+  if (p.chunk == 1) {
+    cudaError_t e = launch_pdl(dk::gdn::gdn_recurrent_kernel<T, DK, DV>,
+                               dim3(p.HV, static_cast<unsigned>(n_seqs), DV / 32), dim3(32 * dk::gdn::kRecWarps), 0, st,
+                               p);
+    if (e != cudaSuccess) return fail(DK_ERR_CUDA, "gdn: launch failed: %s", cudaGetErrorString(e));
+    return DK_OK;
+  }
   static bool done[kMaxDevices] = {};
   auto fn = dk::gdn::gdn_chunk_kernel<T, DK, DV>;
   const int bytes = static_cast<int>(dk::gdn::Smem<DK, DV>::kBytes);

@@ -242,7 +242,8 @@ int dk_attention_batch_invariant_noalloc(const void* q, int64_t q_stride_row, in
  * uses query/key head j / (n_v_heads / n_heads).  Sequences: cu_seqlens (device int64[n_seqs + 1])
  * or, when NULL, n_seqs rows of seq_len tokens each.  initial_state / final_state: [n_seqs,
  * n_v_heads, head_dim_k, head_dim_v] (final in f32), either may be NULL.  chunk_size 64 computes
- * 64-token chunks from each sequence's start (chunked form); 1 steps token by token.  A sequence's
+ * 64-token chunks from each sequence's start (chunked form); 1 steps token by token in the order of
+ * the recurrence (decode path; FLA's fused_recurrent_gated_delta_rule).  A sequence's
  * result never depends on the other sequences of the call.  Head dims: 32/32, 64/64, 128/128. */
 int dk_gdn_forward(const void* q, const void* k, const void* v, const void* g, const void* beta, void* o,
                    const int64_t* cu_seqlens, int64_t n_seqs, int64_t seq_len, int n_heads, int n_v_heads,
