@@ -70,7 +70,11 @@ constexpr int kThreads = 64 + kEpiThreads;        // warp 0 TMA, warp 1 MMA, war
 constexpr int kSlots = 4;
 constexpr int kTmemCols = kSlots * kTileM;        // 512: the whole tensor memory of the SM
 constexpr int kBarrierBytes = 512;
+constexpr int kStagePitch = 33;                   // floats per row of an epilogue transpose tile (32 + 1 pad)
+constexpr int kEpiStageBytes = kEpiWarps * 32 * kStagePitch * 4;   // one 32 x 32 f32 tile per epilogue warp
 constexpr int kSmemBytes = 232448;               // the sm_100 per-CTA maximum
+// [ring (kRingBytes) | barriers].  The FOLD epilogue's transpose tiles take the last
+// kEpiStageBytes of the ring region, so FOLD launches run a shorter ring.
 constexpr int kRingBytes = kSmemBytes - 1024 /*align*/ - kBarrierBytes;
 
 // Stage size for an activation box of a_rows rows: 16 KB of weights + a_rows x 128 B,
@@ -83,8 +87,11 @@ __host__ __device__ __forceinline__ int stage_bytes_for(int a_rows) {
   return ((kWTileBytes + a_rows * kBK * 2 + 1023) / 1024) * 1024;
 }
 __host__ __device__ __forceinline__ int overhang_bytes_for(int a_rows) { return (kTileM - a_rows) * kBK * 2; }
-__host__ __device__ __forceinline__ int stages_for(int a_rows) {
-  const int n = (kRingBytes - overhang_bytes_for(a_rows)) / stage_bytes_for(a_rows);
+__host__ __device__ __forceinline__ int ring_bytes_for(int mode) {
+  return kRingBytes - (mode == 0 /*FOLD*/ ? kEpiStageBytes : 0);
+}
+__host__ __device__ __forceinline__ int stages_for(int a_rows, int mode) {
+  const int n = (ring_bytes_for(mode) - overhang_bytes_for(a_rows)) / stage_bytes_for(a_rows);
   return n < kMaxStages ? n : kMaxStages;
 }
 
@@ -219,6 +226,160 @@ __device__ __forceinline__ void store_silu_mul(const Params& p, T* C, int m, int
   C[static_cast<int64_t>(m) * p.ldc + j] = from_f32<T>(__fmul_rn(s, rnd<T>(u)));
 }
 
+// ---- row-wise epilogue: a warp's 32 columns x 32 tokens, transposed through shared memory so
+// that each lane owns one token row of 32 consecutive columns and writes it with 16-byte stores.
+
+template <typename T>
+__device__ __forceinline__ bool aligned_row(const void* base, int64_t ld, int64_t col) {
+  // 16-byte stores of 8 elements need a 16-byte aligned row start at every row
+  return (reinterpret_cast<uintptr_t>(base) % 16 == 0) && (ld % 8 == 0) && (col % 8 == 0);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_row_vec(T* dst, const float (&v)[32], int count) {
+  // count is 16 or 32 (multiple of 8); dst 16-byte aligned
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (q * 8 < count) {
+      uint4 w;
+      uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const T lo = from_f32<T>(v[q * 8 + 2 * e]), hi = from_f32<T>(v[q * 8 + 2 * e + 1]);
+        wp[e] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
+                (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+      }
+      reinterpret_cast<uint4*>(dst)[q] = w;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void load_row_vec(const T* src, float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 w = reinterpret_cast<const uint4*>(src)[q];
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint16_t lo = static_cast<uint16_t>(wp[e] & 0xffffu), hi = static_cast<uint16_t>(wp[e] >> 16);
+      v[q * 8 + 2 * e] = to_f32<T>(*reinterpret_cast<const T*>(&lo));
+      v[q * 8 + 2 * e + 1] = to_f32<T>(*reinterpret_cast<const T*>(&hi));
+    }
+  }
+}
+
+// Final values of token row m, columns n_base .. n_base + ncols - 1 (ncols <= 32) -> memory.
+template <typename T>
+__device__ __forceinline__ void store_final_row(const Params& p, T* C, int m, int n_base, int ncols, float (&v)[32]) {
+  const dk_matmul_epilogue& e = p.epi;
+  const bool full = (ncols == 32);
+  switch (e.mode) {
+    case DK_EPI_ARGMAX: {
+      unsigned long long best = 0ull;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        if (k < ncols) {
+          const unsigned long long key = argmax_key<T>(v[k], n_base + k);
+          best = key > best ? key : best;
+        }
+      }
+      if (best != 0ull) atomicMax(e.argmax_keys + m, best);
+      if (!C) return;
+      break;   // logits stored as plain values below
+    }
+    case DK_EPI_RESIDUAL: {
+      const T* R = static_cast<const T*>(e.resid) + static_cast<int64_t>(m) * e.ld_resid + n_base;
+      float r[32];
+      if (full && aligned_row<T>(e.resid, e.ld_resid, n_base)) {
+        load_row_vec<T>(R, r);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) r[k] = (k < ncols) ? to_f32<T>(R[k]) : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = __fadd_rn(r[k], rnd<T>(v[k]));
+      break;
+    }
+    case DK_EPI_SILU:
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = silu_f32(rnd<T>(v[k]));
+      break;
+    case DK_EPI_SILU_MUL: {
+      // columns (2j, 2j+1) are (gate, up); outputs n_base / 2 + j
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float s_ = rnd<T>(silu_f32(rnd<T>(v[2 * j])));
+        v[j] = __fmul_rn(s_, rnd<T>(v[2 * j + 1]));
+      }
+      T* dst = C + static_cast<int64_t>(m) * p.ldc + n_base / 2;
+      const int nout = ncols / 2;
+      if (full && aligned_row<T>(C, p.ldc, n_base / 2)) {
+        store_row_vec<T>(dst, v, 16);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < nout) dst[j] = from_f32<T>(v[j]);
+      }
+      return;
+    }
+    case DK_EPI_QKV_CACHE: {
+      if (n_base >= e.q_cols && (e.q_cols % 32) == 0 && (e.head_dim % 32) == 0 && full) {
+        const int j = n_base - e.q_cols;
+        const int which = j / e.kv_cols;
+        const int jj = j - which * e.kv_cols;
+        const int head = jj / e.head_dim, d0 = jj - head * e.head_dim;
+        const int64_t seq = e.row_seq ? e.row_seq[m] : m;
+        T* cache = static_cast<T*>(which == 0 ? e.k_cache : e.v_cache);
+        const int64_t off = seq * e.cache_stride_seq + head * e.cache_stride_head +
+                            static_cast<int64_t>(e.row_pos[m]) * e.cache_stride_tok + d0;
+        if (reinterpret_cast<uintptr_t>(cache + off) % 16 == 0) {
+          store_row_vec<T>(cache + off, v, 32);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) cache[off + k] = from_f32<T>(v[k]);
+        }
+        return;
+      }
+      if (n_base + ncols <= e.q_cols) break;   // all in the q part: plain store below
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        if (k < ncols) store_final<T>(p, C, m, n_base + k, v[k]);
+      return;
+    }
+    default:
+      break;
+  }
+  T* dst = C + static_cast<int64_t>(m) * p.ldc + n_base;
+  if (full && aligned_row<T>(C, p.ldc, n_base)) {
+    store_row_vec<T>(dst, v, 32);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      if (k < ncols) dst[k] = from_f32<T>(v[k]);
+  }
+}
+
+// FOLD: a warp's tile t[j] = final value of (token m_first + j, column n_base + lane), transposed
+// through the warp's stage tile; then lane L handles token m_first + L.  All 32 lanes call this.
+template <typename T>
+__device__ __forceinline__ void emit_rows(const Params& p, T* C, float* stage, int mode, int n_base, int m_first,
+                                          const float (&t)[32]) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) stage[j * kStagePitch + lane] = t[j];
+  __syncwarp();
+  float v[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) v[k] = stage[lane * kStagePitch + k];
+  const int m = m_first + lane;
+  const int ncols = min(32, p.N - n_base);
+  if (m >= p.M || ncols <= 0) return;
+  (void)mode;
+  store_final_row<T>(p, C, m, n_base, ncols, v);
+}
+
 // Thread <-> column n (consecutive columns in consecutive lanes), 32 tokens from m_first.
 // Every lane of the warp calls this (the gate/up exchange is a shuffle).
 template <typename T>
@@ -269,12 +430,14 @@ __device__ __forceinline__ void emit_chunk(const Params& p, T* C, int mode, int 
   }
 }
 
-template <typename T, int FMT>
+// FOLDK: compiled for FOLD launches (final values through the row epilogue); the other
+// schedules use the instantiation without it, which keeps their kernel small.
+template <typename T, int FMT, bool FOLDK>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int n_stages = stages_for(p.a_rows);
+  const int n_stages = stages_for(p.a_rows, p.mode);
   const int stage_bytes = stage_bytes_for(p.a_rows);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingBytes);
   uint64_t* empty = full + kMaxStages;
@@ -423,6 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t use_par = 0;                         // bit k: parity of slot k's fills consumed
     int ordinal = 0;
     T* C = reinterpret_cast<T*>(p.c);
+    float* stage = reinterpret_cast<float*>(smem + kRingBytes - kEpiStageBytes) + (warp - 2) * (32 * kStagePitch);
     const int64_t MN = static_cast<int64_t>(p.M) * p.N;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(col0);
     for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++ordinal) {
@@ -484,7 +648,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(left[j], acc[j]);
           }
           if (last) {
-            emit_chunk<T>(q, C, p.mode, n, n_ok, m0 + c * 32, acc);
+            if constexpr (FOLDK) {
+              emit_rows<T>(q, C, stage, p.mode, nt * kTileN + quarter * 32, m0 + c * 32, acc);
+            } else {
+              // f32 partials: consecutive lanes write consecutive columns (128-byte warp stores)
+              emit_chunk<T>(q, C, p.mode, n, n_ok, m0 + c * 32, acc);
+            }
           } else {
             tmem_st_32x32b_x32(lane_base + static_cast<uint32_t>(res_slot * kTileM) + c * 32, acc);
           }

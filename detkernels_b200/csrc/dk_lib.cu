@@ -309,15 +309,16 @@ int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ld
   const int grid = static_cast<int>(units < sms ? units : sms);
   if (grid <= 0) return DK_OK;
   cudaError_t e;
+  const bool fold = (p.mode == dk::gemm::FOLD);
   if (dtype == DK_BF16) {
-    static bool done[kMaxDevices] = {false};
-    auto fn = dk::gemm::gemm_kernel<__nv_bfloat16, 1>;
-    if ((rc = ensure_smem(fn, dk::gemm::kSmemBytes, done))) return rc;
+    static bool done[2][kMaxDevices] = {};
+    auto fn = fold ? dk::gemm::gemm_kernel<__nv_bfloat16, 1, true> : dk::gemm::gemm_kernel<__nv_bfloat16, 1, false>;
+    if ((rc = ensure_smem(fn, dk::gemm::kSmemBytes, done[fold]))) return rc;
     e = launch_pdl(fn, dim3(grid), dim3(dk::gemm::kThreads), dk::gemm::kSmemBytes, st, tmB, tmA, p);
   } else {
-    static bool done[kMaxDevices] = {false};
-    auto fn = dk::gemm::gemm_kernel<__half, 0>;
-    if ((rc = ensure_smem(fn, dk::gemm::kSmemBytes, done))) return rc;
+    static bool done[2][kMaxDevices] = {};
+    auto fn = fold ? dk::gemm::gemm_kernel<__half, 0, true> : dk::gemm::gemm_kernel<__half, 0, false>;
+    if ((rc = ensure_smem(fn, dk::gemm::kSmemBytes, done[fold]))) return rc;
     e = launch_pdl(fn, dim3(grid), dim3(dk::gemm::kThreads), dk::gemm::kSmemBytes, st, tmB, tmA, p);
   }
   if (e != cudaSuccess) return fail(DK_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
@@ -490,7 +491,7 @@ int dk_kernel_attributes(int which, int* num_regs, int* max_threads, int* local_
   cudaFuncAttributes a{};
   cudaError_t e;
   switch (which) {
-    case 0: e = cudaFuncGetAttributes(&a, dk::gemm::gemm_kernel<__nv_bfloat16, 1>); break;
+    case 0: e = cudaFuncGetAttributes(&a, dk::gemm::gemm_kernel<__nv_bfloat16, 1, true>); break;
     case 1: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 128, 4>); break;
     case 2: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 64, 4>); break;
     case 3: e = cudaFuncGetAttributes(&a, dk::rmsnorm_inv_vec_kernel<float, float, 8>); break;
