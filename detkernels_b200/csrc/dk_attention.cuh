@@ -24,14 +24,17 @@
 // A row's arithmetic therefore depends on its q, its KV sequence and its
 // kv_len only -- not on the batch, the other rows of its tile, or the grid.
 //
-// Work decomposition: one CTA per (row tile, kv head, run of up to `spu`
-// consecutive splits).  A producer warp streams 64-token K/V blocks with TMA
-// (4-D tensor map over the cache, 128- or 64-byte swizzle) into a ring of
-// shared-memory stages that keeps flowing across split boundaries; four
-// consumer warps compute.  When one CTA covers all of a tile's splits it merges
-// them as it goes and writes the output; otherwise each CTA writes its splits'
-// (m, l, O) to the workspace and the last CTA to arrive (atomic counter, no
-// spinning) replays the same split-order merge over them.
+// Work decomposition: a work item is (row tile, kv head, run of up to `spu`
+// consecutive splits).  The grid is persistent (as many CTAs as fit on the GPU
+// at once) and CTA b takes items b, b + grid, ...  A producer warp streams
+// 64-token K/V blocks with TMA (4-D tensor map over the cache, 128- or 64-byte
+// swizzle) into a ring of shared-memory stages that keeps flowing across split
+// AND item boundaries, so the next item's first blocks are in flight while the
+// current one finishes; four consumer warps compute.  When an item covers all of
+// a tile's splits it merges them as it goes and writes the output; otherwise each
+// item writes its splits' (m, l, O) to the workspace and the last to arrive
+// (atomic counter, no spinning) replays the same split-order merge over them.
+// Which CTA computes an item never changes the arithmetic.
 #pragma once
 
 #include "dk_common.cuh"
@@ -187,6 +190,49 @@ __device__ __forceinline__ void merge_split(bool first, float& m, float& l, floa
   m = mn;
 }
 
+// One work item: a row tile, a run of consecutive splits of it, and a kv head.
+struct Item {
+  int tile, unit, kvh;
+  int r0, nr, seq;
+  int max_len, nsplits, s_begin, s_end;
+};
+
+// Decode item w (tile-major, kv head fastest).  Returns 0 for work, 1 when the item's
+// split run is past the tile's last split or the tile is empty (nsplits == 0), 2 for a
+// malformed tile, 3 for a length outside the cache.  Every warp computes the same
+// answer from the same memory.
+__device__ __forceinline__ int describe_item(const Params& p, int64_t w, Item& it) {
+  const int64_t tu = w / p.hkv;
+  it.kvh = static_cast<int>(w - tu * p.hkv);
+  it.tile = static_cast<int>(tu / p.upt);
+  it.unit = static_cast<int>(tu - static_cast<int64_t>(it.tile) * p.upt);
+  if (p.tiles != nullptr) {
+    it.r0 = p.tiles[3 * it.tile + 0];
+    it.nr = p.tiles[3 * it.tile + 1];
+    it.seq = p.tiles[3 * it.tile + 2];
+  } else {
+    it.r0 = it.tile;
+    it.nr = 1;
+    it.seq = it.tile;
+  }
+  it.max_len = 0;
+  it.nsplits = 0;
+  it.s_begin = it.s_end = 0;
+  const int rows_per_tile_max = kRows / p.G;
+  if (it.nr < 1 || it.nr > rows_per_tile_max || it.r0 < 0 || it.r0 + it.nr > p.n_rows || it.seq < 0 ||
+      it.seq >= p.kv_n_seq || it.nr * p.G > p.rows_cap)
+    return 2;
+  for (int i = 0; i < it.nr; ++i) {
+    const int L = p.kv_lens ? p.kv_lens[it.r0 + i] : p.uniform_len;
+    if (L < 0 || L > p.kv_capacity || L > p.max_splits * kSplit) return 3;
+    it.max_len = max(it.max_len, L);
+  }
+  it.nsplits = (it.max_len + kSplit - 1) / kSplit;
+  it.s_begin = it.unit * p.spu;
+  it.s_end = min(it.s_begin + p.spu, it.nsplits);
+  return (it.nsplits == 0 || it.s_begin >= it.nsplits) ? 1 : 0;
+}
+
 // KM: merge elements per consumer thread (ceil(rows x D / 128)); decode launches
 // without row tiles have at most G rows and use a narrow instance.
 template <typename T, int D, int KM>
@@ -207,9 +253,6 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x / p.upt;
-  const int unit = blockIdx.x % p.upt;
-  const int kvh = blockIdx.y;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -225,60 +268,12 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
   }
   pdl_wait();   // lengths, tiles and q may come from the previous kernel
   if (threadIdx.x == 0) pdl_launch_dependents();
+  __syncthreads();   // barrier initialisation visible to every warp
 
-  // ---- tile description (identical in every CTA of the tile) ----
-  int r0, nr, seq;
-  if (p.tiles != nullptr) {
-    r0 = p.tiles[3 * tile + 0];
-    nr = p.tiles[3 * tile + 1];
-    seq = p.tiles[3 * tile + 2];
-  } else {
-    r0 = tile;
-    nr = 1;
-    seq = tile;
-  }
-  const int rows_per_tile_max = kRows / p.G;
-  if (nr < 1 || nr > rows_per_tile_max || r0 < 0 || r0 + nr > p.n_rows || seq < 0 || seq >= p.kv_n_seq ||
-      nr * p.G > p.rows_cap) {
-    if (threadIdx.x == 0 && unit == 0 && kvh == 0) report_error(DK_ERR_DEVICE_CHECK, kDetTile);
-    return;
-  }
-  int max_len = 0;
-  bool len_bad = false;
-  for (int i = 0; i < nr; ++i) {
-    const int L = p.kv_lens ? p.kv_lens[r0 + i] : p.uniform_len;
-    if (L < 0 || L > p.kv_capacity || L > p.max_splits * kSplit) len_bad = true;
-    max_len = max(max_len, L);
-  }
-  if (len_bad) {
-    if (threadIdx.x == 0 && unit == 0 && kvh == 0) report_error(DK_ERR_DEVICE_CHECK, kDetLen);
-    return;
-  }
-  const int nsplits = (max_len + kSplit - 1) / kSplit;
-  const int valid_rows = nr * p.G;
-  T* out = reinterpret_cast<T*>(p.out);
-
-  if (nsplits == 0) {
-    // every row of the tile has an empty KV sequence: output zeros
-    if (unit == 0) {
-      for (int e = threadIdx.x; e < valid_rows * D; e += blockDim.x) {
-        const int rho = e / D, d = e % D;
-        const int i = rho / p.G, gh = rho % p.G;
-        out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(0.0f);
-      }
-    }
-    return;
-  }
-  const int s_begin = unit * p.spu;
-  if (s_begin >= nsplits) return;
-  const int s_end = min(s_begin + p.spu, nsplits);
-  const bool direct = (nsplits <= p.spu);        // this CTA owns every split of the tile
-
-  if (threadIdx.x < kRows) {
-    const int i = threadIdx.x;
-    s_len[i] = (i < nr) ? (p.kv_lens ? p.kv_lens[r0 + i] : p.uniform_len) : 0;
-  }
-  __syncthreads();
+  // Persistent loop over work items (tile, split run, kv head); the producer warp
+  // and the consumer warps walk the same items in the same order, so the producer
+  // streams the next item's blocks while the consumers finish the current one.
+  const int64_t n_items = static_cast<int64_t>(p.n_tiles) * p.upt * p.hkv;
 
   if (warp == kConsumerWarps) {
     // ---------------- producer ----------------
@@ -287,24 +282,28 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
       int stage = 0;
       uint32_t phase = 0;
       int fills = 0;
-      for (int sp = s_begin; sp < s_end && !abort_flag; ++sp) {
-        const int tb = sp * kSplit;
-        const int nblk = (min(tb + kSplit, max_len) - tb + kBlock - 1) / kBlock;
-        for (int b = 0; b < nblk; ++b) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, kDetProdEmpty, abort_flag)) break;
-          uint8_t* st = ring + stage * C::STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          const int t0 = tb + b * kBlock;
+      for (int64_t w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x) {
+        Item it;
+        if (describe_item(p, w, it) != 0) continue;
+        for (int sp = it.s_begin; sp < it.s_end && !abort_flag; ++sp) {
+          const int tb = sp * kSplit;
+          const int nblk = (min(tb + kSplit, it.max_len) - tb + kBlock - 1) / kBlock;
+          for (int b = 0; b < nblk; ++b) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, kDetProdEmpty, abort_flag)) break;
+            uint8_t* st = ring + stage * C::STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            const int t0 = tb + b * kBlock;
 #pragma unroll
-          for (int bx = 0; bx < C::NBOX; ++bx) {
-            tma_load_4d(st + bx * C::BOX_BYTES, &tmK, &full[stage], bx * C::BOXD, t0, kvh, seq);
-            tma_load_4d(st + C::TENSOR_BYTES + bx * C::BOX_BYTES, &tmV, &full[stage], bx * C::BOXD, t0, kvh,
-                        seq);
-          }
-          ++fills;
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1u;
+            for (int bx = 0; bx < C::NBOX; ++bx) {
+              tma_load_4d(st + bx * C::BOX_BYTES, &tmK, &full[stage], bx * C::BOXD, t0, it.kvh, it.seq);
+              tma_load_4d(st + C::TENSOR_BYTES + bx * C::BOX_BYTES, &tmV, &full[stage], bx * C::BOXD, t0, it.kvh,
+                          it.seq);
+            }
+            ++fills;
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
         }
       }
@@ -320,251 +319,282 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
   const int g = lane >> 2;
   const int t4 = lane & 3;
   const int rho0 = g, rho1 = g + 8;
-  const bool v0 = rho0 < valid_rows, v1 = rho1 < valid_rows;
-  const int i0 = v0 ? rho0 / p.G : 0, i1 = v1 ? rho1 / p.G : 0;
   const int ctid = threadIdx.x;  // 0..127
-
-  // Q fragments (A operand, rows rho0/rho1), loaded once.
   constexpr int KC = D / 16;
-  uint32_t qa[KC][4];
-  {
-    const T* q = reinterpret_cast<const T*>(p.q);
-    const T* q0 = v0 ? q + (int64_t)(r0 + i0) * p.q_sr + (int64_t)(kvh * p.G + rho0 % p.G) * p.q_sh : nullptr;
-    const T* q1 = v1 ? q + (int64_t)(r0 + i1) * p.q_sr + (int64_t)(kvh * p.G + rho1 % p.G) * p.q_sh : nullptr;
-#pragma unroll
-    for (int kc = 0; kc < KC; ++kc) {
-      const int d0 = kc * 16 + 2 * t4;
-      qa[kc][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d0) : 0u;
-      qa[kc][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d0) : 0u;
-      qa[kc][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d0 + 8) : 0u;
-      qa[kc][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d0 + 8) : 0u;
-    }
-  }
-
-  // running split-order merge of the elements this thread owns (direct path)
-  float run_m[KM], run_l[KM], run_o[KM];
-#pragma unroll
-  for (int k = 0; k < KM; ++k) {
-    run_m[k] = -INFINITY;
-    run_l[k] = 0.0f;
-    run_o[k] = 0.0f;
-  }
-
   constexpr int NT = D / 8;  // output n-tiles of 8 along d
   const int wr = warp * 16;  // this warp's first token row inside a block
-  const int64_t slot = ((int64_t)tile * p.hkv + kvh) * p.max_splits;
+  T* out = reinterpret_cast<T*>(p.out);
   int stage = 0;
   uint32_t phase = 0;
   uint32_t cphase = 0;
 
-  for (int sp = s_begin; sp < s_end && !abort_flag; ++sp) {
-    const int tok_begin = sp * kSplit;
-    const int tok_end = min(tok_begin + kSplit, max_len);
-    const int nblk = (tok_end - tok_begin + kBlock - 1) / kBlock;
-    const int end0 = v0 ? min(s_len[i0], tok_begin + kSplit) : 0;  // row's own token end in this split
-    const int end1 = v1 ? min(s_len[i1], tok_begin + kSplit) : 0;
-
-    float o[NT][4];
-#pragma unroll
-    for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
-    float m_r[2] = {-INFINITY, -INFINITY};
-    float l_r[2] = {0.0f, 0.0f};
-
-    for (int b = 0; b < nblk; ++b) {
-      if (!mbar_wait(&full[stage], phase, kDetFull, abort_flag)) break;
-      const uint32_t kbase = smem_u32(ring + stage * C::STAGE_BYTES);
-      const uint32_t vbase = kbase + C::TENSOR_BYTES;
-      const int t0 = tok_begin + b * kBlock + wr;  // token of this warp's row 0
-
-      // Tokens no row of the tile may read: zero their V rows (K is masked by select).
-      if (t0 + 16 > tok_end) {
-        uint8_t* vgen = ring + stage * C::STAGE_BYTES + C::TENSOR_BYTES;
-        for (int e = lane; e < 16 * (D / 8); e += 32) {
-          const int rr = e / (D / 8), c = e % (D / 8);
-          if (t0 + rr >= tok_end) {
-            const uint32_t a = chunk_addr<D>(0u, wr + rr, c);
-            *reinterpret_cast<uint4*>(vgen + a) = make_uint4(0u, 0u, 0u, 0u);
-          }
+  for (int64_t w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x) {
+    Item it;
+    const int bad = describe_item(p, w, it);
+    if (bad > 1) {
+      if (ctid == 0 && it.unit == 0 && it.kvh == 0) report_error(DK_ERR_DEVICE_CHECK, bad == 2 ? kDetTile : kDetLen);
+      continue;
+    }
+    const int kvh = it.kvh, r0 = it.r0, nr = it.nr, nsplits = it.nsplits, max_len = it.max_len;
+    const int valid_rows = nr * p.G;
+    if (nsplits == 0) {
+      // every row of the tile has an empty KV sequence: output zeros
+      if (it.unit == 0) {
+        for (int e = ctid; e < valid_rows * D; e += kConsumerWarps * 32) {
+          const int rho = e / D, d = e % D;
+          const int i = rho / p.G, gh = rho % p.G;
+          out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(0.0f);
         }
-        // order these generic-proxy writes before the next TMA write of the stage
-        fence_proxy_async_smem();
-        __syncwarp();
       }
-
-      // S = Q K^T for this warp's 16 tokens (two n-tiles of 8 tokens).
-      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int kc = 0; kc < KC; ++kc) {
-        const int mi = lane >> 3, ri = lane & 7;
-        const int r = wr + (mi >> 1) * 8 + ri;
-        const int c = 2 * kc + (mi & 1);
-        uint32_t b00, b01, b10, b11;
-        ldsm_x4(chunk_addr<D>(kbase, r, c), b00, b01, b10, b11);
-        mma16816<T>(s0, qa[kc], b00, b01);
-        mma16816<T>(s1, qa[kc], b10, b11);
-      }
-
-      // scale, mask, online softmax update (rows rho0 -> s*[0..1], rho1 -> s*[2..3])
-      const int tk = t0 + 2 * t4;
-      float sc[2][4];
-      sc[0][0] = (tk + 0 < end0) ? __fmul_rn(s0[0], p.scale_log2) : -INFINITY;
-      sc[0][1] = (tk + 1 < end0) ? __fmul_rn(s0[1], p.scale_log2) : -INFINITY;
-      sc[0][2] = (tk + 8 < end0) ? __fmul_rn(s1[0], p.scale_log2) : -INFINITY;
-      sc[0][3] = (tk + 9 < end0) ? __fmul_rn(s1[1], p.scale_log2) : -INFINITY;
-      sc[1][0] = (tk + 0 < end1) ? __fmul_rn(s0[2], p.scale_log2) : -INFINITY;
-      sc[1][1] = (tk + 1 < end1) ? __fmul_rn(s0[3], p.scale_log2) : -INFINITY;
-      sc[1][2] = (tk + 8 < end1) ? __fmul_rn(s1[2], p.scale_log2) : -INFINITY;
-      sc[1][3] = (tk + 9 < end1) ? __fmul_rn(s1[3], p.scale_log2) : -INFINITY;
-
-      uint32_t pa[4];
-      float alpha[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float mx = fmaxf(fmaxf(sc[h][0], sc[h][1]), fmaxf(sc[h][2], sc[h][3]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_r[h], mx);
-        const float mref = (m_new == -INFINITY) ? 0.0f : m_new;
-        alpha[h] = weight_of(m_r[h], mref);
-        float pr[4];
-        const uint32_t lo = pack_round<T>(weight_of(sc[h][0], mref), weight_of(sc[h][1], mref), pr[0], pr[1]);
-        const uint32_t hi = pack_round<T>(weight_of(sc[h][2], mref), weight_of(sc[h][3], mref), pr[2], pr[3]);
-        pa[h] = lo;      // a0 (row g) / a1 (row g+8): tokens 2t, 2t+1
-        pa[h + 2] = hi;  // a2 / a3: tokens 8+2t, 8+2t+1
-        const float psum = __fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3]));
-        l_r[h] = __fadd_rn(__fmul_rn(l_r[h], alpha[h]), psum);
-        m_r[h] = m_new;
-      }
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        o[j][0] = __fmul_rn(o[j][0], alpha[0]);
-        o[j][1] = __fmul_rn(o[j][1], alpha[0]);
-        o[j][2] = __fmul_rn(o[j][2], alpha[1]);
-        o[j][3] = __fmul_rn(o[j][3], alpha[1]);
-      }
-      // O += P V
-#pragma unroll
-      for (int pc = 0; pc < D / 16; ++pc) {
-        const int mi = lane >> 3, ri = lane & 7;
-        const int r = wr + (mi & 1) * 8 + ri;
-        const int c = 2 * pc + (mi >> 1);
-        uint32_t b0a, b1a, b0b, b1b;
-        ldsm_x4_t(chunk_addr<D>(vbase, r, c), b0a, b1a, b0b, b1b);
-        mma16816<T>(o[2 * pc], pa, b0a, b1a);
-        mma16816<T>(o[2 * pc + 1], pa, b0b, b1b);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-      if (++stage == C::STAGES) {
-        stage = 0;
-        phase ^= 1u;
-      }
+      continue;
     }
+    if (bad == 1) continue;  // no split of this tile falls in this item's run
+    const int s_begin = it.s_begin, s_end = it.s_end;
+    const bool direct = (nsplits <= p.spu);        // this item owns every split of the tile
 
-    // quad-reduce l (fixed butterfly; m is already quad-uniform)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 1));
-      l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 2));
-    }
-
-    // ---- merge the four warps of this split in warp order ----
-    if (!csync(cbar, cphase, abort_flag)) break;   // the previous split's merge reads are done
-    if (v0) {
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-        *reinterpret_cast<float2*>(comb_o + (warp * p.rows_cap + rho0) * C::CSTRIDE + j * 8 + 2 * t4) =
-            make_float2(o[j][0], o[j][1]);
-      if (t4 == 0) {
-        comb_ml[(warp * p.rows_cap + rho0) * 2 + 0] = m_r[0];
-        comb_ml[(warp * p.rows_cap + rho0) * 2 + 1] = l_r[0];
-      }
-    }
-    if (v1) {
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-        *reinterpret_cast<float2*>(comb_o + (warp * p.rows_cap + rho1) * C::CSTRIDE + j * 8 + 2 * t4) =
-            make_float2(o[j][2], o[j][3]);
-      if (t4 == 0) {
-        comb_ml[(warp * p.rows_cap + rho1) * 2 + 0] = m_r[1];
-        comb_ml[(warp * p.rows_cap + rho1) * 2 + 1] = l_r[1];
-      }
-    }
+    // the previous item's readers of s_len are done; refresh it
+    if (!csync(cbar, cphase, abort_flag)) break;
+    if (ctid < kRows) s_len[ctid] = (ctid < nr) ? (p.kv_lens ? p.kv_lens[r0 + ctid] : p.uniform_len) : 0;
     if (!csync(cbar, cphase, abort_flag)) break;
 
+    const bool v0 = rho0 < valid_rows, v1 = rho1 < valid_rows;
+    const int i0 = v0 ? rho0 / p.G : 0, i1 = v1 ? rho1 / p.G : 0;
+
+    // Q fragments (A operand, rows rho0/rho1), loaded once per item.
+    uint32_t qa[KC][4];
+    {
+      const T* q = reinterpret_cast<const T*>(p.q);
+      const T* q0 = v0 ? q + (int64_t)(r0 + i0) * p.q_sr + (int64_t)(kvh * p.G + rho0 % p.G) * p.q_sh : nullptr;
+      const T* q1 = v1 ? q + (int64_t)(r0 + i1) * p.q_sr + (int64_t)(kvh * p.G + rho1 % p.G) * p.q_sh : nullptr;
+#pragma unroll
+      for (int kc = 0; kc < KC; ++kc) {
+        const int d0 = kc * 16 + 2 * t4;
+        qa[kc][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d0) : 0u;
+        qa[kc][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d0) : 0u;
+        qa[kc][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d0 + 8) : 0u;
+        qa[kc][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d0 + 8) : 0u;
+      }
+    }
+
+    // running split-order merge of the elements this thread owns (direct path)
+    float run_m[KM], run_l[KM], run_o[KM];
 #pragma unroll
     for (int k = 0; k < KM; ++k) {
-      const int e = ctid + k * (kConsumerWarps * 32);
-      if (e < valid_rows * D) {
-        const int rho = e / D, d = e % D;
-        float mw[kConsumerWarps];
-        float M = -INFINITY;
+      run_m[k] = -INFINITY;
+      run_l[k] = 0.0f;
+      run_o[k] = 0.0f;
+    }
+    const int64_t slot = ((int64_t)it.tile * p.hkv + kvh) * p.max_splits;
+
+    for (int sp = s_begin; sp < s_end && !abort_flag; ++sp) {
+      const int tok_begin = sp * kSplit;
+      const int tok_end = min(tok_begin + kSplit, max_len);
+      const int nblk = (tok_end - tok_begin + kBlock - 1) / kBlock;
+      const int end0 = v0 ? min(s_len[i0], tok_begin + kSplit) : 0;  // row's own token end in this split
+      const int end1 = v1 ? min(s_len[i1], tok_begin + kSplit) : 0;
+
+      float o[NT][4];
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-          mw[w] = comb_ml[(w * p.rows_cap + rho) * 2];
-          M = fmaxf(M, mw[w]);
+      for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+      float m_r[2] = {-INFINITY, -INFINITY};
+      float l_r[2] = {0.0f, 0.0f};
+
+      for (int b = 0; b < nblk; ++b) {
+        if (!mbar_wait(&full[stage], phase, kDetFull, abort_flag)) break;
+        const uint32_t kbase = smem_u32(ring + stage * C::STAGE_BYTES);
+        const uint32_t vbase = kbase + C::TENSOR_BYTES;
+        const int t0 = tok_begin + b * kBlock + wr;  // token of this warp's row 0
+
+        // Tokens no row of the tile may read: zero their V rows (K is masked by select).
+        if (t0 + 16 > tok_end) {
+          uint8_t* vgen = ring + stage * C::STAGE_BYTES + C::TENSOR_BYTES;
+          for (int e = lane; e < 16 * (D / 8); e += 32) {
+            const int rr = e / (D / 8), c = e % (D / 8);
+            if (t0 + rr >= tok_end) {
+              const uint32_t a = chunk_addr<D>(0u, wr + rr, c);
+              *reinterpret_cast<uint4*>(vgen + a) = make_uint4(0u, 0u, 0u, 0u);
+            }
+          }
+          // order these generic-proxy writes before the next TMA write of the stage
+          fence_proxy_async_smem();
+          __syncwarp();
         }
-        const float mref = (M == -INFINITY) ? 0.0f : M;
-        float L = 0.0f, O = 0.0f;
+
+        // S = Q K^T for this warp's 16 tokens (two n-tiles of 8 tokens).
+        float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-          const float wt = weight_of(mw[w], mref);
-          L = __fadd_rn(L, __fmul_rn(comb_ml[(w * p.rows_cap + rho) * 2 + 1], wt));
-          O = __fadd_rn(O, __fmul_rn(comb_o[(w * p.rows_cap + rho) * C::CSTRIDE + d], wt));
+        for (int kc = 0; kc < KC; ++kc) {
+          const int mi = lane >> 3, ri = lane & 7;
+          const int r = wr + (mi >> 1) * 8 + ri;
+          const int c = 2 * kc + (mi & 1);
+          uint32_t b00, b01, b10, b11;
+          ldsm_x4(chunk_addr<D>(kbase, r, c), b00, b01, b10, b11);
+          mma16816<T>(s0, qa[kc], b00, b01);
+          mma16816<T>(s1, qa[kc], b10, b11);
         }
-        if (direct) {
-          const int own = (s_len[rho / p.G] + kSplit - 1) / kSplit;
-          if (sp < own) merge_split(sp == 0, run_m[k], run_l[k], run_o[k], M, L, O);
-        } else {
-          const int64_t base = (slot + sp) * p.rows_cap + rho;
-          p.ws_o[base * D + d] = O;
-          if (d == 0) {
-            p.ws_ml[base * 2 + 0] = M;
-            p.ws_ml[base * 2 + 1] = L;
+
+        // scale, mask, online softmax update (rows rho0 -> s*[0..1], rho1 -> s*[2..3])
+        const int tk = t0 + 2 * t4;
+        float sc[2][4];
+        sc[0][0] = (tk + 0 < end0) ? __fmul_rn(s0[0], p.scale_log2) : -INFINITY;
+        sc[0][1] = (tk + 1 < end0) ? __fmul_rn(s0[1], p.scale_log2) : -INFINITY;
+        sc[0][2] = (tk + 8 < end0) ? __fmul_rn(s1[0], p.scale_log2) : -INFINITY;
+        sc[0][3] = (tk + 9 < end0) ? __fmul_rn(s1[1], p.scale_log2) : -INFINITY;
+        sc[1][0] = (tk + 0 < end1) ? __fmul_rn(s0[2], p.scale_log2) : -INFINITY;
+        sc[1][1] = (tk + 1 < end1) ? __fmul_rn(s0[3], p.scale_log2) : -INFINITY;
+        sc[1][2] = (tk + 8 < end1) ? __fmul_rn(s1[2], p.scale_log2) : -INFINITY;
+        sc[1][3] = (tk + 9 < end1) ? __fmul_rn(s1[3], p.scale_log2) : -INFINITY;
+
+        uint32_t pa[4];
+        float alpha[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float mx = fmaxf(fmaxf(sc[h][0], sc[h][1]), fmaxf(sc[h][2], sc[h][3]));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          const float m_new = fmaxf(m_r[h], mx);
+          const float mref = (m_new == -INFINITY) ? 0.0f : m_new;
+          alpha[h] = weight_of(m_r[h], mref);
+          float pr[4];
+          const uint32_t lo = pack_round<T>(weight_of(sc[h][0], mref), weight_of(sc[h][1], mref), pr[0], pr[1]);
+          const uint32_t hi = pack_round<T>(weight_of(sc[h][2], mref), weight_of(sc[h][3], mref), pr[2], pr[3]);
+          pa[h] = lo;      // a0 (row g) / a1 (row g+8): tokens 2t, 2t+1
+          pa[h + 2] = hi;  // a2 / a3: tokens 8+2t, 8+2t+1
+          const float psum = __fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3]));
+          l_r[h] = __fadd_rn(__fmul_rn(l_r[h], alpha[h]), psum);
+          m_r[h] = m_new;
+        }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          o[j][0] = __fmul_rn(o[j][0], alpha[0]);
+          o[j][1] = __fmul_rn(o[j][1], alpha[0]);
+          o[j][2] = __fmul_rn(o[j][2], alpha[1]);
+          o[j][3] = __fmul_rn(o[j][3], alpha[1]);
+        }
+        // O += P V
+#pragma unroll
+        for (int pc = 0; pc < D / 16; ++pc) {
+          const int mi = lane >> 3, ri = lane & 7;
+          const int r = wr + (mi & 1) * 8 + ri;
+          const int c = 2 * pc + (mi >> 1);
+          uint32_t b0a, b1a, b0b, b1b;
+          ldsm_x4_t(chunk_addr<D>(vbase, r, c), b0a, b1a, b0b, b1b);
+          mma16816<T>(o[2 * pc], pa, b0a, b1a);
+          mma16816<T>(o[2 * pc + 1], pa, b0b, b1b);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == C::STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+
+      // quad-reduce l (fixed butterfly; m is already quad-uniform)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 1));
+        l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 2));
+      }
+
+      // ---- merge the four warps of this split in warp order ----
+      if (!csync(cbar, cphase, abort_flag)) break;   // the previous split's merge reads are done
+      if (v0) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+          *reinterpret_cast<float2*>(comb_o + (warp * p.rows_cap + rho0) * C::CSTRIDE + j * 8 + 2 * t4) =
+              make_float2(o[j][0], o[j][1]);
+        if (t4 == 0) {
+          comb_ml[(warp * p.rows_cap + rho0) * 2 + 0] = m_r[0];
+          comb_ml[(warp * p.rows_cap + rho0) * 2 + 1] = l_r[0];
+        }
+      }
+      if (v1) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+          *reinterpret_cast<float2*>(comb_o + (warp * p.rows_cap + rho1) * C::CSTRIDE + j * 8 + 2 * t4) =
+              make_float2(o[j][2], o[j][3]);
+        if (t4 == 0) {
+          comb_ml[(warp * p.rows_cap + rho1) * 2 + 0] = m_r[1];
+          comb_ml[(warp * p.rows_cap + rho1) * 2 + 1] = l_r[1];
+        }
+      }
+      if (!csync(cbar, cphase, abort_flag)) break;
+
+#pragma unroll
+      for (int k = 0; k < KM; ++k) {
+        const int e = ctid + k * (kConsumerWarps * 32);
+        if (e < valid_rows * D) {
+          const int rho = e / D, d = e % D;
+          float mw[kConsumerWarps];
+          float M = -INFINITY;
+#pragma unroll
+          for (int w = 0; w < kConsumerWarps; ++w) {
+            mw[w] = comb_ml[(w * p.rows_cap + rho) * 2];
+            M = fmaxf(M, mw[w]);
+          }
+          const float mref = (M == -INFINITY) ? 0.0f : M;
+          float L = 0.0f, O = 0.0f;
+#pragma unroll
+          for (int w = 0; w < kConsumerWarps; ++w) {
+            const float wt = weight_of(mw[w], mref);
+            L = __fadd_rn(L, __fmul_rn(comb_ml[(w * p.rows_cap + rho) * 2 + 1], wt));
+            O = __fadd_rn(O, __fmul_rn(comb_o[(w * p.rows_cap + rho) * C::CSTRIDE + d], wt));
+          }
+          if (direct) {
+            const int own = (s_len[rho / p.G] + kSplit - 1) / kSplit;
+            if (sp < own) merge_split(sp == 0, run_m[k], run_l[k], run_o[k], M, L, O);
+          } else {
+            const int64_t base = (slot + sp) * p.rows_cap + rho;
+            p.ws_o[base * D + d] = O;
+            if (d == 0) {
+              p.ws_ml[base * 2 + 0] = M;
+              p.ws_ml[base * 2 + 1] = L;
+            }
           }
         }
       }
     }
-  }
-  if (abort_flag) return;
+    if (abort_flag) break;
 
-  if (!direct) {
-    // ---- the last CTA of this (tile, kv head) replays the split-order merge ----
-    __threadfence();
-    if (!csync(cbar, cphase, abort_flag)) return;
-    if (ctid == 0) {
-      const int arrivals = (nsplits + p.spu - 1) / p.spu;
-      const int old = atomicAdd(p.counters + (int64_t)tile * p.hkv + kvh, 1);
-      const bool last = (old == arrivals - 1);
-      s_misc[0] = last ? 1 : 0;
-      if (last) p.counters[(int64_t)tile * p.hkv + kvh] = 0;
+    if (!direct) {
+      // ---- the last CTA of this (tile, kv head) replays the split-order merge ----
+      __threadfence();
+      if (!csync(cbar, cphase, abort_flag)) break;
+      if (ctid == 0) {
+        const int arrivals = (nsplits + p.spu - 1) / p.spu;
+        const int old = atomicAdd(p.counters + (int64_t)it.tile * p.hkv + kvh, 1);
+        const bool last = (old == arrivals - 1);
+        s_misc[0] = last ? 1 : 0;
+        if (last) p.counters[(int64_t)it.tile * p.hkv + kvh] = 0;
+      }
+      if (!csync(cbar, cphase, abort_flag)) break;
+      if (s_misc[0] == 0) continue;
+      __threadfence();
+#pragma unroll
+      for (int k = 0; k < KM; ++k) {
+        const int e = ctid + k * (kConsumerWarps * 32);
+        if (e < valid_rows * D) {
+          const int rho = e / D, d = e % D;
+          const int own = (s_len[rho / p.G] + kSplit - 1) / kSplit;
+          for (int s = 0; s < own; ++s) {
+            const int64_t base = (slot + s) * p.rows_cap + rho;
+            merge_split(s == 0, run_m[k], run_l[k], run_o[k], __ldcg(p.ws_ml + base * 2), __ldcg(p.ws_ml + base * 2 + 1),
+                        __ldcg(p.ws_o + base * D + d));
+          }
+        }
+      }
     }
-    if (!csync(cbar, cphase, abort_flag)) return;
-    if (s_misc[0] == 0) return;
-    __threadfence();
+
 #pragma unroll
     for (int k = 0; k < KM; ++k) {
       const int e = ctid + k * (kConsumerWarps * 32);
       if (e < valid_rows * D) {
         const int rho = e / D, d = e % D;
-        const int own = (s_len[rho / p.G] + kSplit - 1) / kSplit;
-        for (int s = 0; s < own; ++s) {
-          const int64_t base = (slot + s) * p.rows_cap + rho;
-          merge_split(s == 0, run_m[k], run_l[k], run_o[k], __ldcg(p.ws_ml + base * 2), __ldcg(p.ws_ml + base * 2 + 1),
-                      __ldcg(p.ws_o + base * D + d));
-        }
+        const int i = rho / p.G, gh = rho % p.G;
+        const float r = (s_len[i] == 0) ? 0.0f : __fdiv_rn(run_o[k], run_l[k]);
+        out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(r);
       }
-    }
-  }
-
-#pragma unroll
-  for (int k = 0; k < KM; ++k) {
-    const int e = ctid + k * (kConsumerWarps * 32);
-    if (e < valid_rows * D) {
-      const int rho = e / D, d = e % D;
-      const int i = rho / p.G, gh = rho % p.G;
-      const float r = (s_len[i] == 0) ? 0.0f : __fdiv_rn(run_o[k], run_l[k]);
-      out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(r);
     }
   }
 }

@@ -381,26 +381,42 @@ AttnPlan plan_attention(int32_t n_tiles, int32_t rows_per_tile, int32_t hq, int3
 }
 
 template <typename T, int D, int KM>
-int attn_launch_km(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int grid_x, int grid_y,
+int attn_launch_km(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int64_t n_items,
                    cudaStream_t st) {
   using C = dk::attn::Cfg<D>;
   static bool done[kMaxDevices] = {false};
+  static int resident[kMaxDevices][dk::attn::kRows + 1] = {};   // CTAs per SM, by rows_cap
   auto fn = dk::attn::attn_kernel<T, D, KM>;
   int rc = ensure_smem(fn, C::smem_bytes(dk::attn::kRows), done);
   if (rc) return rc;
-  cudaError_t e = launch_pdl(fn, dim3(grid_x, grid_y), dim3(dk::attn::kThreads), C::smem_bytes(p.rows_cap), st, tk,
-                             tv, p);
+  const int dev = current_device();
+  const int smem = C::smem_bytes(p.rows_cap);
+  int per_sm = 0;
+  if (dev >= 0 && dev < kMaxDevices && p.rows_cap >= 0 && p.rows_cap <= dk::attn::kRows)
+    per_sm = resident[dev][p.rows_cap];
+  if (per_sm <= 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, dk::attn::kThreads, smem) != cudaSuccess ||
+        per_sm <= 0)
+      per_sm = 1;
+    if (dev >= 0 && dev < kMaxDevices && p.rows_cap >= 0 && p.rows_cap <= dk::attn::kRows)
+      resident[dev][p.rows_cap] = per_sm;
+  }
+  // persistent grid: every CTA resident at once, each walking items b, b + grid, ...
+  const int64_t cap = static_cast<int64_t>(per_sm) * sm_count(dev);
+  const int grid = static_cast<int>(n_items < cap ? n_items : cap);
+  if (grid <= 0) return DK_OK;
+  cudaError_t e = launch_pdl(fn, dim3(grid), dim3(dk::attn::kThreads), smem, st, tk, tv, p);
   if (e != cudaSuccess) return fail(DK_ERR_CUDA, "attention_batch_invariant: launch failed: %s", cudaGetErrorString(e));
   return DK_OK;
 }
 
 template <typename T, int D>
-int attn_launch(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int grid_x, int grid_y,
+int attn_launch(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int64_t n_items,
                 cudaStream_t st) {
   constexpr int kThr = dk::attn::kConsumerWarps * 32;
   constexpr int kNarrow = (4 < dk::attn::Cfg<D>::KMAX) ? 4 : dk::attn::Cfg<D>::KMAX;
-  if (p.rows_cap * D <= kNarrow * kThr) return attn_launch_km<T, D, kNarrow>(tk, tv, p, grid_x, grid_y, st);
-  return attn_launch_km<T, D, dk::attn::Cfg<D>::KMAX>(tk, tv, p, grid_x, grid_y, st);
+  if (p.rows_cap * D <= kNarrow * kThr) return attn_launch_km<T, D, kNarrow>(tk, tv, p, n_items, st);
+  return attn_launch_km<T, D, dk::attn::Cfg<D>::KMAX>(tk, tv, p, n_items, st);
 }
 
 template <typename T, int DK, int DV>
@@ -885,16 +901,15 @@ int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_
   if (rc) return rc;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int gx = pl.n_tiles * pl.upt;
-  const int gy = n_kv_heads;
+  const int64_t n_items = static_cast<int64_t>(pl.n_tiles) * pl.upt * n_kv_heads;
   if (dtype == DK_BF16) {
-    if (head_dim == 32) return attn_launch<__nv_bfloat16, 32>(tk, tv, p, gx, gy, st);
-    if (head_dim == 64) return attn_launch<__nv_bfloat16, 64>(tk, tv, p, gx, gy, st);
-    return attn_launch<__nv_bfloat16, 128>(tk, tv, p, gx, gy, st);
+    if (head_dim == 32) return attn_launch<__nv_bfloat16, 32>(tk, tv, p, n_items, st);
+    if (head_dim == 64) return attn_launch<__nv_bfloat16, 64>(tk, tv, p, n_items, st);
+    return attn_launch<__nv_bfloat16, 128>(tk, tv, p, n_items, st);
   }
-  if (head_dim == 32) return attn_launch<__half, 32>(tk, tv, p, gx, gy, st);
-  if (head_dim == 64) return attn_launch<__half, 64>(tk, tv, p, gx, gy, st);
-  return attn_launch<__half, 128>(tk, tv, p, gx, gy, st);
+  if (head_dim == 32) return attn_launch<__half, 32>(tk, tv, p, n_items, st);
+  if (head_dim == 64) return attn_launch<__half, 64>(tk, tv, p, n_items, st);
+  return attn_launch<__half, 128>(tk, tv, p, n_items, st);
 }
 
 size_t dk_attention_variant_workspace_size(int32_t batch, int32_t n_heads, int32_t head_dim) {
