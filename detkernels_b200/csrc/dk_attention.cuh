@@ -47,6 +47,8 @@ constexpr int kBlock = 64;
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);
 constexpr int kRows = 16;
+constexpr int kItemSlots = 2;   // work items staged ahead of the consumers
+constexpr int kItemInts = 32;   // ints per staged item: description [0, 11), kv lengths [16, 32)
 
 template <int D>
 struct Cfg {
@@ -64,7 +66,8 @@ struct Cfg {
   static constexpr int KMAX = (kRows * D + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32);
   // dynamic shared memory for a launch whose tiles hold up to `rows` mma rows
   static __host__ __device__ int smem_bytes(int rows) {
-    return 1024 + RING_BYTES + kConsumerWarps * rows * (CSTRIDE + 2) * 4 + 512;
+    return 1024 + RING_BYTES + kConsumerWarps * rows * (CSTRIDE + 2) * 4 + 512 +
+           kItemSlots * (kItemInts * 4 + rows * D * 2 + 16) + 128;
   }
 };
 
@@ -95,6 +98,7 @@ enum : int {
   kDetFull = 0x201,
   kDetSync = 0x202,
   kDetDrain = 0x203,
+  kDetItem = 0x204,
   kDetLen = 0x210,   // a kv_len exceeds the cache capacity or max_kv_len
   kDetTile = 0x211,  // a row tile is malformed
 };
@@ -168,9 +172,18 @@ __device__ __forceinline__ bool csync(uint64_t* bar, uint32_t& phase, bool& abor
   return ok;
 }
 
+// 2^x with the single-instruction hardware approximation (relative error < 2^-22);
+// 2^-inf = +0 and 2^0 = 1 exactly.  Every weight of the softmax and of both merges
+// goes through this one function.
+__device__ __forceinline__ float exp2_hw(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float weight_of(float m, float mref) {
   // exp2(m - mref); m == -inf gives 0.
-  return exp2f(__fsub_rn(m, mref));
+  return exp2_hw(__fsub_rn(m, mref));
 }
 
 // One step of the split-order merge: (m, l, o) <- merge((m, l, o), (ms, ls, os)).
@@ -248,8 +261,14 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
       (reinterpret_cast<uintptr_t>(comb_ml + kConsumerWarps * p.rows_cap * 2) + 7) & ~uintptr_t(7));
   uint64_t* empty = full + C::STAGES;
   uint64_t* cbar = empty + C::STAGES;
-  int* s_len = reinterpret_cast<int*>(cbar + 1);   // kv_len of each tile row [16]
-  int* s_misc = s_len + kRows;                      // [0] last-arriver flag
+  int* s_misc = reinterpret_cast<int*>(cbar + 1);  // [0] last-arriver flag
+  // item ring: per slot the item description and its rows' kv lengths, and the tile's q rows
+  int* islot = s_misc + 16;                                                  // [kItemSlots][kItemInts]
+  T* iq = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(islot + kItemSlots * kItemInts) + 15) &
+                               ~uintptr_t(15));                              // [kItemSlots][rows_cap][D]
+  uint64_t* ifull = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(iq + kItemSlots * p.rows_cap * D) + 7) & ~uintptr_t(7));
+  uint64_t* iempty = ifull + kItemSlots;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -260,6 +279,10 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
       mbar_init(&empty[s], kConsumerWarps);
     }
     mbar_init(cbar, kConsumerWarps * 32);
+    for (int s = 0; s < kItemSlots; ++s) {
+      mbar_init(&ifull[s], 31);
+      mbar_init(&iempty[s], kConsumerWarps);
+    }
     fence_mbar_init();
   }
   if (warp == kConsumerWarps && lane == 0) {
@@ -310,6 +333,59 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
       bool drain_abort = false;
       for (int f = (fills > C::STAGES ? fills - C::STAGES : 0); f < fills; ++f)
         mbar_wait(&full[f % C::STAGES], static_cast<uint32_t>((f / C::STAGES) & 1), kDetDrain, drain_abort);
+    } else {
+      // lanes 1..31: stage each item's description, kv lengths and q rows in the item ring,
+      // up to kItemSlots items ahead of the consumers
+      bool abort_flag = false;
+      const int ml = lane - 1;
+      int slot = 0;
+      uint32_t iphase = 0;
+      const T* q = reinterpret_cast<const T*>(p.q);
+      for (int64_t w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x) {
+        if (!mbar_wait(&iempty[slot], iphase ^ 1u, kDetItem, abort_flag)) break;
+        Item it;
+        const int bad = describe_item(p, w, it);
+        int* m = islot + slot * kItemInts;
+        if (ml == 0) {
+          m[0] = bad;
+          m[1] = it.tile;
+          m[2] = it.unit;
+          m[3] = it.kvh;
+          m[4] = it.r0;
+          m[5] = it.nr;
+          m[6] = it.seq;
+          m[7] = it.max_len;
+          m[8] = it.nsplits;
+          m[9] = it.s_begin;
+          m[10] = it.s_end;
+        }
+        if (ml < kRows) m[16 + ml] = (bad <= 1 && ml < it.nr) ? (p.kv_lens ? p.kv_lens[it.r0 + ml] : p.uniform_len) : 0;
+        if (bad == 0) {
+          T* qs = iq + slot * p.rows_cap * D;
+          const int chunks = it.nr * p.G * (D / 8);
+          for (int e = ml; e < chunks; e += 31) {
+            const int rho = e / (D / 8), c = e - rho * (D / 8);
+            const int i = rho / p.G, gh = rho - i * p.G;
+            const T* src = q + (int64_t)(it.r0 + i) * p.q_sr + (int64_t)(it.kvh * p.G + gh) * p.q_sh + c * 8;
+            uint4 v;
+            if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+              v = *reinterpret_cast<const uint4*>(src);
+            } else {
+              uint16_t h[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) h[j] = reinterpret_cast<const uint16_t*>(src)[j];
+              v = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16), h[4] | (uint32_t(h[5]) << 16),
+                             h[6] | (uint32_t(h[7]) << 16));
+            }
+            *reinterpret_cast<uint4*>(qs + rho * D + c * 8) = v;
+          }
+        }
+        mbar_arrive(&ifull[slot]);
+        if (++slot == kItemSlots) {
+          slot = 0;
+          iphase ^= 1u;
+        }
+      }
     }
     return;  // the producer warp takes no part in the merges
   }
@@ -328,52 +404,58 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
   uint32_t phase = 0;
   uint32_t cphase = 0;
 
+  // ldmatrix source offsets inside a stage's K and V tensors (fixed per thread)
+  uint32_t k_off[KC], v_off[D / 16];
+  {
+    const int mi = lane >> 3, ri = lane & 7;
+#pragma unroll
+    for (int kc = 0; kc < KC; ++kc) k_off[kc] = chunk_addr<D>(0u, wr + (mi >> 1) * 8 + ri, 2 * kc + (mi & 1));
+#pragma unroll
+    for (int pc = 0; pc < D / 16; ++pc) v_off[pc] = chunk_addr<D>(0u, wr + (mi & 1) * 8 + ri, 2 * pc + (mi >> 1));
+  }
+  int islot_i = 0;
+  uint32_t iph = 0;
   for (int64_t w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x) {
-    Item it;
-    const int bad = describe_item(p, w, it);
+    if (!mbar_wait(&ifull[islot_i], iph, kDetItem, abort_flag)) break;
+    const int* m = islot + islot_i * kItemInts;
+    const int* s_len = m + 16;   // kv length of each tile row
+    const T* qs = iq + islot_i * p.rows_cap * D;
+    do {
+    const int bad = m[0];
+    const int tile = m[1], unit = m[2], kvh = m[3], r0 = m[4], nr = m[5];
+    const int max_len = m[7], nsplits = m[8];
     if (bad > 1) {
-      if (ctid == 0 && it.unit == 0 && it.kvh == 0) report_error(DK_ERR_DEVICE_CHECK, bad == 2 ? kDetTile : kDetLen);
-      continue;
+      if (ctid == 0 && unit == 0 && kvh == 0) report_error(DK_ERR_DEVICE_CHECK, bad == 2 ? kDetTile : kDetLen);
+      break;
     }
-    const int kvh = it.kvh, r0 = it.r0, nr = it.nr, nsplits = it.nsplits, max_len = it.max_len;
     const int valid_rows = nr * p.G;
     if (nsplits == 0) {
       // every row of the tile has an empty KV sequence: output zeros
-      if (it.unit == 0) {
+      if (unit == 0) {
         for (int e = ctid; e < valid_rows * D; e += kConsumerWarps * 32) {
           const int rho = e / D, d = e % D;
           const int i = rho / p.G, gh = rho % p.G;
           out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(0.0f);
         }
       }
-      continue;
+      break;
     }
-    if (bad == 1) continue;  // no split of this tile falls in this item's run
-    const int s_begin = it.s_begin, s_end = it.s_end;
+    if (bad == 1) break;  // no split of this tile falls in this item's run
+    const int s_begin = m[9], s_end = m[10];
     const bool direct = (nsplits <= p.spu);        // this item owns every split of the tile
-
-    // the previous item's readers of s_len are done; refresh it
-    if (!csync(cbar, cphase, abort_flag)) break;
-    if (ctid < kRows) s_len[ctid] = (ctid < nr) ? (p.kv_lens ? p.kv_lens[r0 + ctid] : p.uniform_len) : 0;
-    if (!csync(cbar, cphase, abort_flag)) break;
 
     const bool v0 = rho0 < valid_rows, v1 = rho1 < valid_rows;
     const int i0 = v0 ? rho0 / p.G : 0, i1 = v1 ? rho1 / p.G : 0;
 
-    // Q fragments (A operand, rows rho0/rho1), loaded once per item.
+    // Q fragments (A operand, rows rho0/rho1) from the staged q rows.
     uint32_t qa[KC][4];
-    {
-      const T* q = reinterpret_cast<const T*>(p.q);
-      const T* q0 = v0 ? q + (int64_t)(r0 + i0) * p.q_sr + (int64_t)(kvh * p.G + rho0 % p.G) * p.q_sh : nullptr;
-      const T* q1 = v1 ? q + (int64_t)(r0 + i1) * p.q_sr + (int64_t)(kvh * p.G + rho1 % p.G) * p.q_sh : nullptr;
 #pragma unroll
-      for (int kc = 0; kc < KC; ++kc) {
-        const int d0 = kc * 16 + 2 * t4;
-        qa[kc][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d0) : 0u;
-        qa[kc][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d0) : 0u;
-        qa[kc][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d0 + 8) : 0u;
-        qa[kc][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d0 + 8) : 0u;
-      }
+    for (int kc = 0; kc < KC; ++kc) {
+      const int d0 = kc * 16 + 2 * t4;
+      qa[kc][0] = v0 ? *reinterpret_cast<const uint32_t*>(qs + rho0 * D + d0) : 0u;
+      qa[kc][1] = v1 ? *reinterpret_cast<const uint32_t*>(qs + rho1 * D + d0) : 0u;
+      qa[kc][2] = v0 ? *reinterpret_cast<const uint32_t*>(qs + rho0 * D + d0 + 8) : 0u;
+      qa[kc][3] = v1 ? *reinterpret_cast<const uint32_t*>(qs + rho1 * D + d0 + 8) : 0u;
     }
 
     // running split-order merge of the elements this thread owns (direct path)
@@ -384,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
       run_l[k] = 0.0f;
       run_o[k] = 0.0f;
     }
-    const int64_t slot = ((int64_t)it.tile * p.hkv + kvh) * p.max_splits;
+    const int64_t slot = ((int64_t)tile * p.hkv + kvh) * p.max_splits;
 
     for (int sp = s_begin; sp < s_end && !abort_flag; ++sp) {
       const int tok_begin = sp * kSplit;
@@ -424,11 +506,8 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
         float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kc = 0; kc < KC; ++kc) {
-          const int mi = lane >> 3, ri = lane & 7;
-          const int r = wr + (mi >> 1) * 8 + ri;
-          const int c = 2 * kc + (mi & 1);
           uint32_t b00, b01, b10, b11;
-          ldsm_x4(chunk_addr<D>(kbase, r, c), b00, b01, b10, b11);
+          ldsm_x4(kbase + k_off[kc], b00, b01, b10, b11);
           mma16816<T>(s0, qa[kc], b00, b01);
           mma16816<T>(s1, qa[kc], b10, b11);
         }
@@ -436,14 +515,24 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
         // scale, mask, online softmax update (rows rho0 -> s*[0..1], rho1 -> s*[2..3])
         const int tk = t0 + 2 * t4;
         float sc[2][4];
-        sc[0][0] = (tk + 0 < end0) ? __fmul_rn(s0[0], p.scale_log2) : -INFINITY;
-        sc[0][1] = (tk + 1 < end0) ? __fmul_rn(s0[1], p.scale_log2) : -INFINITY;
-        sc[0][2] = (tk + 8 < end0) ? __fmul_rn(s1[0], p.scale_log2) : -INFINITY;
-        sc[0][3] = (tk + 9 < end0) ? __fmul_rn(s1[1], p.scale_log2) : -INFINITY;
-        sc[1][0] = (tk + 0 < end1) ? __fmul_rn(s0[2], p.scale_log2) : -INFINITY;
-        sc[1][1] = (tk + 1 < end1) ? __fmul_rn(s0[3], p.scale_log2) : -INFINITY;
-        sc[1][2] = (tk + 8 < end1) ? __fmul_rn(s1[2], p.scale_log2) : -INFINITY;
-        sc[1][3] = (tk + 9 < end1) ? __fmul_rn(s1[3], p.scale_log2) : -INFINITY;
+        sc[0][0] = __fmul_rn(s0[0], p.scale_log2);
+        sc[0][1] = __fmul_rn(s0[1], p.scale_log2);
+        sc[0][2] = __fmul_rn(s1[0], p.scale_log2);
+        sc[0][3] = __fmul_rn(s1[1], p.scale_log2);
+        sc[1][0] = __fmul_rn(s0[2], p.scale_log2);
+        sc[1][1] = __fmul_rn(s0[3], p.scale_log2);
+        sc[1][2] = __fmul_rn(s1[2], p.scale_log2);
+        sc[1][3] = __fmul_rn(s1[3], p.scale_log2);
+        if (tk + 9 >= end0 || tk + 9 >= end1) {   // some of this thread's tokens are past a row's end
+          if (tk + 0 >= end0) sc[0][0] = -INFINITY;
+          if (tk + 1 >= end0) sc[0][1] = -INFINITY;
+          if (tk + 8 >= end0) sc[0][2] = -INFINITY;
+          if (tk + 9 >= end0) sc[0][3] = -INFINITY;
+          if (tk + 0 >= end1) sc[1][0] = -INFINITY;
+          if (tk + 1 >= end1) sc[1][1] = -INFINITY;
+          if (tk + 8 >= end1) sc[1][2] = -INFINITY;
+          if (tk + 9 >= end1) sc[1][3] = -INFINITY;
+        }
 
         uint32_t pa[4];
         float alpha[2];
@@ -464,21 +553,20 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
           l_r[h] = __fadd_rn(__fmul_rn(l_r[h], alpha[h]), psum);
           m_r[h] = m_new;
         }
+        if (alpha[0] != 1.0f || alpha[1] != 1.0f) {   // multiplying by exactly 1 changes nothing
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          o[j][0] = __fmul_rn(o[j][0], alpha[0]);
-          o[j][1] = __fmul_rn(o[j][1], alpha[0]);
-          o[j][2] = __fmul_rn(o[j][2], alpha[1]);
-          o[j][3] = __fmul_rn(o[j][3], alpha[1]);
+          for (int j = 0; j < NT; ++j) {
+            o[j][0] = __fmul_rn(o[j][0], alpha[0]);
+            o[j][1] = __fmul_rn(o[j][1], alpha[0]);
+            o[j][2] = __fmul_rn(o[j][2], alpha[1]);
+            o[j][3] = __fmul_rn(o[j][3], alpha[1]);
+          }
         }
         // O += P V
 #pragma unroll
         for (int pc = 0; pc < D / 16; ++pc) {
-          const int mi = lane >> 3, ri = lane & 7;
-          const int r = wr + (mi & 1) * 8 + ri;
-          const int c = 2 * pc + (mi >> 1);
           uint32_t b0a, b1a, b0b, b1b;
-          ldsm_x4_t(chunk_addr<D>(vbase, r, c), b0a, b1a, b0b, b1b);
+          ldsm_x4_t(vbase + v_off[pc], b0a, b1a, b0b, b1b);
           mma16816<T>(o[2 * pc], pa, b0a, b1a);
           mma16816<T>(o[2 * pc + 1], pa, b0b, b1b);
         }
@@ -563,13 +651,13 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
       if (!csync(cbar, cphase, abort_flag)) break;
       if (ctid == 0) {
         const int arrivals = (nsplits + p.spu - 1) / p.spu;
-        const int old = atomicAdd(p.counters + (int64_t)it.tile * p.hkv + kvh, 1);
+        const int old = atomicAdd(p.counters + (int64_t)tile * p.hkv + kvh, 1);
         const bool last = (old == arrivals - 1);
         s_misc[0] = last ? 1 : 0;
-        if (last) p.counters[(int64_t)it.tile * p.hkv + kvh] = 0;
+        if (last) p.counters[(int64_t)tile * p.hkv + kvh] = 0;
       }
       if (!csync(cbar, cphase, abort_flag)) break;
-      if (s_misc[0] == 0) continue;
+      if (s_misc[0] == 0) break;
       __threadfence();
 #pragma unroll
       for (int k = 0; k < KM; ++k) {
@@ -595,6 +683,14 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
         const float r = (s_len[i] == 0) ? 0.0f : __fdiv_rn(run_o[k], run_l[k]);
         out[(int64_t)(r0 + i) * p.o_sr + (int64_t)(kvh * p.G + gh) * p.o_sh + d] = from_f32<T>(r);
       }
+    }
+    } while (0);
+    // this warp is done with the staged item: release its slot
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&iempty[islot_i]);
+    if (++islot_i == kItemSlots) {
+      islot_i = 0;
+      iph ^= 1u;
     }
   }
 }

@@ -79,6 +79,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// try_wait with a suspend-time hint (ns): the thread is suspended until the phase with
+// `parity` completes or the hint expires.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -105,7 +119,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int de
   const unsigned long long t0 = globaltimer_ns();
 #pragma unroll 1
   while (true) {
-    if (mbar_try_wait(b, parity)) return true;
+    // the thread sleeps in hardware until the phase completes or ~1 us passes, so a
+    // waiting warp takes no issue slots from the working ones and wakes on completion
+    if (mbar_try_wait_sleep(b, parity, 1000u)) return true;
     if (device_failed()) {
       abort_flag = true;
       return false;
