@@ -506,10 +506,15 @@ def main(argv=None):
     ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the end-to-end public-API timing")
     ap.add_argument("--skip-gdn", action="store_true", help="skip the gated-delta-rule section")
+    ap.add_argument("--gdn-only", action="store_true", help="run and print only the gated-delta-rule section")
     ap.add_argument("--new-tokens", type=int, default=NEW_TOKENS,
                     help="tokens generated per prompt (the workload is 128; smaller only for profiling)")
     args = ap.parse_args(argv)
     NEW_TOKENS = args.new_tokens
+    if args.gdn_only:
+        peaks, _ = load_peaks()
+        print(json.dumps({"gdn": gdn_bench(peaks)}), flush=True)
+        return 0
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         return run_reference(args, rank, int(os.environ.get("WORLD_SIZE", "1")))
