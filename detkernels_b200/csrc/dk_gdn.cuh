@@ -9,7 +9,7 @@
 //
 // (the published gated delta rule; query/key head of value head j is
 // j / (HV / H)).  Chunked form used here, for a chunk of L <= 64 tokens that
-// starts with state S0, gamma_t = g_0 + ... + g_t (inclusive, in token order):
+// starts with state S0, gamma_t = g_0 + ... + g_t (inclusive; a fixed-order scan):
 //
 //     A_tj = beta_t exp(gamma_t - gamma_j) k_t.k_j           (j < t)
 //     R_t  = beta_t (v_t - exp(gamma_t) S0^T k_t)
@@ -115,36 +115,82 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Params p) 
     const int L = static_cast<int>((len - c0) < p.chunk ? (len - c0) : p.chunk);
     __syncthreads();  // previous chunk done with every tile
     // ---- load the chunk: K^T, Q^T (f32), V, g, beta; rows >= L are zero ----
-    for (int e = tid; e < kChunk * DK; e += kThreads) {
-      const int t = e / DK, i = e - t * DK;
-      float kv = 0.0f, qv = 0.0f;
-      if (t < L) {
-        const int64_t off = ((bos + c0 + t) * p.H + hq) * DK + i;
-        kv = to_f32<T>(k[off]);
-        qv = to_f32<T>(q[off]);
-      }
-      Kt[i * kPadC + t] = kv;
-      Qt[i * kPadC + t] = qv;
-    }
-    for (int e = tid; e < kChunk * DV; e += kThreads) {
-      const int t = e / DV, c = e - t * DV;
-      Vp[e] = (t < L) ? to_f32<T>(v[((bos + c0 + t) * HV + hv) * DV + c]) : 0.0f;
-    }
-    if (tid < 32) {
-      // gamma: inclusive prefix sum in token order (one lane, fixed order)
-      if (tid == 0) {
-        float acc = 0.0f;
-        for (int t = 0; t < kChunk; ++t) {
-          if (t < L) acc = __fadd_rn(acc, load_any(p.g, (bos + c0 + t) * HV + hv, p.gb_dtype));
-          gam[t] = acc;
+    // Every thread issues all of its 16-byte loads before using any of them.
+    {
+      constexpr int KCH = kChunk * DK / 8;   // 16-byte chunks of the K (and Q) tile
+      constexpr int VCH = kChunk * DV / 8;
+      constexpr int KPT = (KCH + kThreads - 1) / kThreads;
+      constexpr int VPT = (VCH + kThreads - 1) / kThreads;
+      uint4 kr[KPT], qr[KPT], vr[VPT];
+      // K/Q: token index fastest across lanes, so the transposed shared-memory stores
+      // (row stride kPadC = 68 floats) fall in 32 different banks
+#pragma unroll
+      for (int u = 0; u < KPT; ++u) {
+        const int e = tid + u * kThreads;
+        const int t = e % kChunk, c = e / kChunk;
+        kr[u] = qr[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (e < KCH && t < L) {
+          const int64_t off = ((bos + c0 + t) * p.H + hq) * DK + c * 8;
+          kr[u] = *reinterpret_cast<const uint4*>(k + off);
+          qr[u] = *reinterpret_cast<const uint4*>(q + off);
         }
       }
-      __syncwarp();
-      for (int t = tid; t < kChunk; t += 32) {
-        egam[t] = expf(gam[t]);
-        bet[t] = (t < L) ? load_any(p.beta, (bos + c0 + t) * HV + hv, p.gb_dtype) : 0.0f;
-        wlast[t] = (t < L) ? expf(__fsub_rn(gam[L - 1], gam[t])) : 0.0f;
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) {
+        const int e = tid + u * kThreads;
+        const int t = e / (DV / 8), c = e - t * (DV / 8);
+        vr[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (e < VCH && t < L) vr[u] = *reinterpret_cast<const uint4*>(v + ((bos + c0 + t) * HV + hv) * DV + c * 8);
       }
+      // g and beta of the chunk, one token per thread of the first two warps
+      float gt = 0.0f, bt = 0.0f;
+      if (tid < kChunk && tid < L) {
+        gt = load_any(p.g, (bos + c0 + tid) * HV + hv, p.gb_dtype);
+        bt = load_any(p.beta, (bos + c0 + tid) * HV + hv, p.gb_dtype);
+      }
+#pragma unroll
+      for (int u = 0; u < KPT; ++u) {
+        const int e = tid + u * kThreads;
+        if (e < KCH) {
+          const int t = e % kChunk, c = e / kChunk;
+          const T* kh = reinterpret_cast<const T*>(&kr[u]);
+          const T* qh = reinterpret_cast<const T*>(&qr[u]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            Kt[(c * 8 + j) * kPadC + t] = to_f32<T>(kh[j]);
+            Qt[(c * 8 + j) * kPadC + t] = to_f32<T>(qh[j]);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) {
+        const int e = tid + u * kThreads;
+        if (e < VCH) {
+          const T* vh = reinterpret_cast<const T*>(&vr[u]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) Vp[e * 8 + j] = to_f32<T>(vh[j]);
+        }
+      }
+      // gamma: inclusive prefix sum over the chunk in a fixed order -- a Kogge-Stone scan
+      // within each 32-token half, then the first half's total added to the second half
+      if (tid < kChunk) {
+        const int ln = tid & 31;
+        float acc = gt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float up = __shfl_up_sync(0xffffffffu, acc, o);
+          if (ln >= o) acc = __fadd_rn(up, acc);
+        }
+        gam[tid] = acc;
+        bet[tid] = bt;
+      }
+    }
+    __syncthreads();
+    if (tid >= 32 && tid < kChunk) gam[tid] = __fadd_rn(gam[31], gam[tid]);
+    __syncthreads();
+    if (tid < kChunk) {
+      egam[tid] = expf(gam[tid]);
+      wlast[tid] = (tid < L) ? expf(__fsub_rn(gam[L - 1], gam[tid])) : 0.0f;
     }
     __syncthreads();
 

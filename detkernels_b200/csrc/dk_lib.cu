@@ -1038,6 +1038,8 @@ int dk_gdn_forward(const void* q, const void* k, const void* v, const void* g, c
   if (!(scale == scale)) return fail(DK_ERR_INVALID_ARGUMENT, "%s: scale is NaN", what);
   if (n_seqs == 0) return DK_OK;
   if (!q || !k || !v || !g || !beta || !o) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null tensor", what);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v))
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: q, k and v must start on a 16-byte boundary", what);
   dk::gdn::Params p{};
   p.q = q;
   p.k = k;

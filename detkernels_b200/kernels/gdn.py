@@ -73,7 +73,9 @@ def _forward(q, k, v, g, beta, scale, initial_state, output_final_state, cu_seql
         initial_state = initial_state.contiguous()
     if scale is None:
         scale = K ** -0.5
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    # contiguous, starting on a 16-byte boundary (a fresh copy when a view is not)
+    q, k, v = (t.contiguous() for t in (q, k, v))
+    q, k, v = (t if t.data_ptr() % 16 == 0 else t.clone() for t in (q, k, v))
     gb = g.dtype if g.dtype == beta.dtype else torch.float32
     g, beta = g.to(gb).contiguous(), beta.to(gb).contiguous()
     o = torch.empty((B, T, HV, V), device=q.device, dtype=q.dtype)

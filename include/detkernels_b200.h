@@ -238,7 +238,8 @@ int dk_attention_batch_invariant_noalloc(const void* q, int64_t q_stride_row, in
  * replaces the FLA `chunk_gated_delta_rule` / `fused_recurrent_gated_delta_rule` calls of the
  * reference's gdn/repro.py:76,161-162,293-294 (fla 0.5.1 API, [B, T, heads, dim] layout).
  * q, k: [tokens, n_heads, head_dim_k]; v: [tokens, n_v_heads, head_dim_v]; g (log decay), beta:
- * [tokens, n_v_heads]; o: [tokens, n_v_heads, head_dim_v] in q's dtype, all contiguous.  Value head j
+ * [tokens, n_v_heads]; o: [tokens, n_v_heads, head_dim_v] in q's dtype, all contiguous, q/k/v
+ * starting on a 16-byte boundary.  Value head j
  * uses query/key head j / (n_v_heads / n_heads).  Sequences: cu_seqlens (device int64[n_seqs + 1])
  * or, when NULL, n_seqs rows of seq_len tokens each.  initial_state / final_state: [n_seqs,
  * n_v_heads, head_dim_k, head_dim_v] (final in f32), either may be NULL.  chunk_size 64 computes
