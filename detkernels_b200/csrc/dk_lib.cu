@@ -9,6 +9,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <utility>
 
 #include "dk_common.cuh"
@@ -17,6 +18,7 @@
 #include "dk_attention.cuh"
 #include "dk_attention_variant.cuh"
 #include "dk_gdn.cuh"
+#include "dk_gdn_tc.cuh"
 
 namespace {
 
@@ -438,8 +440,25 @@ int gdn_launch_t(const dk::gdn::Params& p, int64_t n_seqs, cudaStream_t st) {
   return DK_OK;
 }
 
+template <int D>
+int gdn_launch_tc(const dk::gdn::Params& p, int64_t n_seqs, cudaStream_t st) {
+  static bool done[kMaxDevices] = {};
+  auto fn = dk::gdn::gdn_chunk_tc_kernel<D>;
+  const int bytes = dk::gdn::TcSmem<D>::kBytes;
+  int rc = ensure_smem(fn, bytes, done);
+  if (rc) return rc;
+  cudaError_t e = launch_pdl(fn, dim3(p.HV, static_cast<unsigned>(n_seqs)), dim3(dk::gdn::kTcThreads), bytes, st, p);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "gdn: launch failed: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
+
 template <typename T>
 int gdn_launch_dims(const dk::gdn::Params& p, int dk_, int dv_, int64_t n_seqs, cudaStream_t st) {
+  // chunked bf16 with head dims 64/128: tensor-core kernel; otherwise the f32 CUDA-core kernel
+  if (std::is_same<T, __nv_bfloat16>::value && p.chunk == dk::gdn::kChunk && dk_ == dv_) {
+    if (dk_ == 128) return gdn_launch_tc<128>(p, n_seqs, st);
+    if (dk_ == 64) return gdn_launch_tc<64>(p, n_seqs, st);
+  }
   if (dk_ == 128 && dv_ == 128) return gdn_launch_t<T, 128, 128>(p, n_seqs, st);
   if (dk_ == 64 && dv_ == 64) return gdn_launch_t<T, 64, 64>(p, n_seqs, st);
   if (dk_ == 32 && dv_ == 32) return gdn_launch_t<T, 32, 32>(p, n_seqs, st);

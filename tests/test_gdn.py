@@ -117,3 +117,16 @@ def test_repro_cli_writes_the_reference_report(dev, tmp_path):
     rep = json.loads(out.read_text())
     for key in ("row_results", "packing_results", "decode_results", "geometry_results"):
         assert rep[key] and all(c["identical"] for r in rep[key] for c in r["comparisons"])
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_f16_inputs_match_oracle(dev, D):
+    """f16 inputs (the f32 CUDA-core chunk kernel) against the oracle."""
+    import torch
+    from detkernels_b200.kernels.gdn import chunk_gated_delta_rule
+    q, k, v, gate, beta, cu, s0 = _inputs(dev, [70, 129], 2, 4, D, torch.float16, seed=11, h0=True)
+    o, final = chunk_gated_delta_rule(q, k, v, gate, beta, initial_state=s0, output_final_state=True, cu_seqlens=cu)
+    want_o, want_s = oracle.gdn_recurrent(_np(q[0]), _np(k[0]), _np(v[0]), _np(gate[0]), _np(beta[0]),
+                                          initial_state=_np(s0), cu_seqlens=cu.cpu().numpy(), dtype="float32")
+    np.testing.assert_allclose(_np(o[0]), want_o, rtol=2 ** -9, atol=4e-3)
+    np.testing.assert_allclose(_np(final), want_s, rtol=S_RTOL, atol=S_ATOL)
