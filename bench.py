@@ -242,10 +242,10 @@ def gemm_vs_cublas(iters=10):
 
 
 # DRAM bytes (read + write) per algorithmic byte of the decode attention kernel, from an ncu
-# capture of `python -m detkernels_b200.kernels.benchmark` (B=64, H=8, S=2048, D=64: 268.4 MB
-# of K/V per launch); the kernel reads each KV byte once, so traffic scales with the
-# algorithmic bytes of a launch.  Set from profiles/attention_decode_b64_h8_s2048_d64.md.
-ATTN_DRAM_PER_ALGO_BYTE = 1.0
+# capture of `python -m detkernels_b200.kernels.benchmark` (B=64, H=8, S=2048, D=64: 270.21 MB
+# of DRAM traffic for 268.57 MB algorithmic); the kernel reads each KV byte once, so traffic
+# scales with the algorithmic bytes of a launch.
+ATTN_DRAM_PER_ALGO_BYTE = 270.21 / 268.57
 
 
 # ----------------------------------------------------------------------------- gated delta rule
