@@ -191,8 +191,9 @@ class TinyModel:
 
         ragged = isinstance(prompt_token_ids, (list, tuple))
         if kernel_set == "batch_invariant" and str(self.device).startswith("cuda"):
-            prompts = ([list(map(int, p)) for p in prompt_token_ids] if ragged
-                       else [[int(t)] for t in prompt_token_ids.tolist()])
+            # ragged prompts go to the engine as given (any int sequence; the plan reads them
+            # with numpy); a (B,) tensor becomes B one-token prompts
+            prompts = (list(prompt_token_ids) if ragged else [[int(t)] for t in prompt_token_ids.tolist()])
             cap = max(len(p) for p in prompts) + n_steps
             eng = self.engine(len(prompts), cap)
             return eng.generate(prompts, n_steps)
@@ -325,34 +326,39 @@ class DecodeEngine:
         """Device-side description of a prefill: every prompt token is a row."""
         import torch
 
+        import numpy as np
+
         dev = self.device
         B = len(prompts)
         assert 0 < B <= self.B, "batch exceeds engine capacity"
         G = self.H // self.Hkv
         rows_per_tile = 16 // G
-        seq_idx, pos_idx, tiles, last = [], [], [], []
-        for b, p in enumerate(prompts):
-            assert 0 < len(p) <= self.S, "prompt longer than engine capacity"
-            for t0 in range(0, len(p), rows_per_tile):
-                n = min(rows_per_tile, len(p) - t0)
-                tiles.append((len(seq_idx), n, b))
-                seq_idx += [b] * n
-                pos_idx += list(range(t0, t0 + n))
-            last.append(len(seq_idx) - 1)
+        lens = np.fromiter((len(p) for p in prompts), dtype=np.int64, count=B)
+        assert (lens > 0).all() and (lens <= self.S).all(), "prompt longer than engine capacity"
+        tok = np.concatenate([np.asarray(p, dtype=np.int64).reshape(-1) for p in prompts])
+        starts = np.cumsum(lens) - lens                       # first row of each prompt
+        rows = np.repeat(np.arange(B, dtype=np.int64), lens)  # row -> prompt
+        pos = np.arange(tok.size, dtype=np.int64) - np.repeat(starts, lens)
+        # tiles of up to rows_per_tile consecutive rows of one prompt: (first row, rows, prompt)
+        n_t = (lens + rows_per_tile - 1) // rows_per_tile
+        t_b = np.repeat(np.arange(B, dtype=np.int64), n_t)
+        t_k = np.arange(int(n_t.sum()), dtype=np.int64) - np.repeat(np.cumsum(n_t) - n_t, n_t)
+        tiles = np.stack([starts[t_b] + t_k * rows_per_tile,
+                          np.minimum(rows_per_tile, lens[t_b] - t_k * rows_per_tile), t_b], axis=1)
         host = {
-            "tok": torch.tensor([t for p in prompts for t in p], dtype=torch.long),
-            "rows": torch.tensor(seq_idx, dtype=torch.long),
-            "pos": torch.tensor(pos_idx, dtype=torch.long),
-            "tiles": torch.tensor(tiles, dtype=torch.int32),
-            "last": torch.tensor(last, dtype=torch.long),
-            "lens": torch.tensor([len(p) for p in prompts], dtype=torch.int32),
+            "tok": torch.from_numpy(tok),
+            "rows": torch.from_numpy(rows),
+            "pos": torch.from_numpy(pos),
+            "tiles": torch.from_numpy(tiles.astype(np.int32)),
+            "last": torch.from_numpy(starts + lens - 1),
+            "lens": torch.from_numpy(lens.astype(np.int32)),
         }
         plan = {k: v.pin_memory().to(dev, non_blocking=True) for k, v in host.items()}
         plan["q_lens"] = (plan["pos"] + 1).to(torch.int32)
         plan["rows32"] = plan["rows"].to(torch.int32)
         plan["pos32"] = plan["pos"].to(torch.int32)
         plan["B"] = B
-        plan["max_len"] = max(len(p) for p in prompts)
+        plan["max_len"] = int(lens.max())
         plan["h2d_bytes"] = sum(v.numel() * v.element_size() for v in host.values())
         lib = self._lib.load()
         R = host["tok"].numel()
