@@ -134,6 +134,24 @@ __device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// The low / high 16-bit element of a packed pair as f32.
+template <typename T>
+__device__ __forceinline__ float lo_f32(uint32_t v);
+template <typename T>
+__device__ __forceinline__ float hi_f32(uint32_t v);
+template <>
+__device__ __forceinline__ float lo_f32<__nv_bfloat16>(uint32_t v) { return __uint_as_float(v << 16); }
+template <>
+__device__ __forceinline__ float hi_f32<__nv_bfloat16>(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+template <>
+__device__ __forceinline__ float lo_f32<__half>(uint32_t v) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xffffu)));
+}
+template <>
+__device__ __forceinline__ float hi_f32<__half>(uint32_t v) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
+}
+
 // Round two probabilities to the input type, pack them, and return the rounded values.
 template <typename T>
 __device__ __forceinline__ uint32_t pack_round(float lo, float hi, float& rlo, float& rhi);
@@ -248,7 +266,14 @@ __device__ __forceinline__ int describe_item(const Params& p, int64_t w, Item& i
 
 // KM: merge elements per consumer thread (ceil(rows x D / 128)); decode launches
 // without row tiles have at most G rows and use a narrow instance.
-template <typename T, int D, int KM>
+// T1: launches whose tiles hold one mma row (rows_cap == 1: decode without grouped
+// query heads).  The products are formed transposed -- S^T = K q^T and O^T = V^T P^T,
+// the 16 tokens of a warp as the MMA's M dimension instead of 15 idle query rows --
+// which halves the MMAs and the accumulator.  Every sum keeps the 16-row form's
+// operands and order (per token the same 16-deep MMA dot products over the same
+// k steps; l from the same four tokens per lane, (p0 + p1) + (p2 + p3), and the
+// same butterfly), so a row's bits are those of the 16-row form.
+template <typename T, int D, int KM, bool T1>
 __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
     attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const Params p) {
   using C = Cfg<D>;
@@ -408,10 +433,16 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
   uint32_t k_off[KC], v_off[D / 16];
   {
     const int mi = lane >> 3, ri = lane & 7;
+    // K as the B operand (two n-tiles of 8 tokens) or, for T1, as the A operand (16
+    // tokens x 16 d); V the other way round (ldmatrix.trans either way)
+    const int r_a = wr + (mi & 1) * 8 + ri, c_a = mi >> 1;
+    const int r_b = wr + (mi >> 1) * 8 + ri, c_b = mi & 1;
 #pragma unroll
-    for (int kc = 0; kc < KC; ++kc) k_off[kc] = chunk_addr<D>(0u, wr + (mi >> 1) * 8 + ri, 2 * kc + (mi & 1));
+    for (int kc = 0; kc < KC; ++kc)
+      k_off[kc] = T1 ? chunk_addr<D>(0u, r_a, 2 * kc + c_a) : chunk_addr<D>(0u, r_b, 2 * kc + c_b);
 #pragma unroll
-    for (int pc = 0; pc < D / 16; ++pc) v_off[pc] = chunk_addr<D>(0u, wr + (mi & 1) * 8 + ri, 2 * pc + (mi >> 1));
+    for (int pc = 0; pc < D / 16; ++pc)
+      v_off[pc] = T1 ? chunk_addr<D>(0u, r_b, 2 * pc + c_b) : chunk_addr<D>(0u, r_a, 2 * pc + c_a);
   }
   int islot_i = 0;
   uint32_t iph = 0;
@@ -447,15 +478,22 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
     const bool v0 = rho0 < valid_rows, v1 = rho1 < valid_rows;
     const int i0 = v0 ? rho0 / p.G : 0, i1 = v1 ? rho1 / p.G : 0;
 
-    // Q fragments (A operand, rows rho0/rho1) from the staged q rows.
+    // Q fragments (A operand, rows rho0/rho1) from the staged q rows; for T1 the B
+    // operand q^T (column g = query row g: only column 0 is a row)
     uint32_t qa[KC][4];
 #pragma unroll
     for (int kc = 0; kc < KC; ++kc) {
       const int d0 = kc * 16 + 2 * t4;
-      qa[kc][0] = v0 ? *reinterpret_cast<const uint32_t*>(qs + rho0 * D + d0) : 0u;
-      qa[kc][1] = v1 ? *reinterpret_cast<const uint32_t*>(qs + rho1 * D + d0) : 0u;
-      qa[kc][2] = v0 ? *reinterpret_cast<const uint32_t*>(qs + rho0 * D + d0 + 8) : 0u;
-      qa[kc][3] = v1 ? *reinterpret_cast<const uint32_t*>(qs + rho1 * D + d0 + 8) : 0u;
+      if constexpr (T1) {
+        qa[kc][0] = v0 ? *reinterpret_cast<const uint32_t*>(qs + d0) : 0u;
+        qa[kc][1] = v0 ? *reinterpret_cast<const uint32_t*>(qs + d0 + 8) : 0u;
+        qa[kc][2] = qa[kc][3] = 0u;
+      } else {
+        qa[kc][0] = v0 ? *reinterpret_cast<const uint32_t*>(qs + rho0 * D + d0) : 0u;
+        qa[kc][1] = v1 ? *reinterpret_cast<const uint32_t*>(qs + rho1 * D + d0) : 0u;
+        qa[kc][2] = v0 ? *reinterpret_cast<const uint32_t*>(qs + rho0 * D + d0 + 8) : 0u;
+        qa[kc][3] = v1 ? *reinterpret_cast<const uint32_t*>(qs + rho1 * D + d0 + 8) : 0u;
+      }
     }
 
     // running split-order merge of the elements this thread owns (direct path)
@@ -475,9 +513,12 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
       const int end0 = v0 ? min(s_len[i0], tok_begin + kSplit) : 0;  // row's own token end in this split
       const int end1 = v1 ? min(s_len[i1], tok_begin + kSplit) : 0;
 
-      float o[NT][4];
+      // O (NT n-tiles of 8 d) or, for T1, O^T (D / 16 m-tiles of 16 d; column 0 = the row)
+      constexpr int NO = T1 ? D / 16 : NT;
+      float o[NO][4];
 #pragma unroll
-      for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+      for (int j = 0; j < NO; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+      const int end_t1 = min(s_len[0], tok_begin + kSplit);   // T1: the row's token end in this split
       float m_r[2] = {-INFINITY, -INFINITY};
       float l_r[2] = {0.0f, 0.0f};
 
@@ -502,73 +543,125 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
           __syncwarp();
         }
 
-        // S = Q K^T for this warp's 16 tokens (two n-tiles of 8 tokens).
-        float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (T1) {
+          // S^T = K q^T: c[0] = token t0 + g, c[2] = token t0 + g + 8 (column 2*t4: only t4 == 0 is the row)
+          float st[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int kc = 0; kc < KC; ++kc) {
-          uint32_t b00, b01, b10, b11;
-          ldsm_x4(kbase + k_off[kc], b00, b01, b10, b11);
-          mma16816<T>(s0, qa[kc], b00, b01);
-          mma16816<T>(s1, qa[kc], b10, b11);
-        }
-
-        // scale, mask, online softmax update (rows rho0 -> s*[0..1], rho1 -> s*[2..3])
-        const int tk = t0 + 2 * t4;
-        float sc[2][4];
-        sc[0][0] = __fmul_rn(s0[0], p.scale_log2);
-        sc[0][1] = __fmul_rn(s0[1], p.scale_log2);
-        sc[0][2] = __fmul_rn(s1[0], p.scale_log2);
-        sc[0][3] = __fmul_rn(s1[1], p.scale_log2);
-        sc[1][0] = __fmul_rn(s0[2], p.scale_log2);
-        sc[1][1] = __fmul_rn(s0[3], p.scale_log2);
-        sc[1][2] = __fmul_rn(s1[2], p.scale_log2);
-        sc[1][3] = __fmul_rn(s1[3], p.scale_log2);
-        if (tk + 9 >= end0 || tk + 9 >= end1) {   // some of this thread's tokens are past a row's end
-          if (tk + 0 >= end0) sc[0][0] = -INFINITY;
-          if (tk + 1 >= end0) sc[0][1] = -INFINITY;
-          if (tk + 8 >= end0) sc[0][2] = -INFINITY;
-          if (tk + 9 >= end0) sc[0][3] = -INFINITY;
-          if (tk + 0 >= end1) sc[1][0] = -INFINITY;
-          if (tk + 1 >= end1) sc[1][1] = -INFINITY;
-          if (tk + 8 >= end1) sc[1][2] = -INFINITY;
-          if (tk + 9 >= end1) sc[1][3] = -INFINITY;
-        }
-
-        uint32_t pa[4];
-        float alpha[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float mx = fmaxf(fmaxf(sc[h][0], sc[h][1]), fmaxf(sc[h][2], sc[h][3]));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          const float m_new = fmaxf(m_r[h], mx);
-          const float mref = (m_new == -INFINITY) ? 0.0f : m_new;
-          alpha[h] = weight_of(m_r[h], mref);
-          float pr[4];
-          const uint32_t lo = pack_round<T>(weight_of(sc[h][0], mref), weight_of(sc[h][1], mref), pr[0], pr[1]);
-          const uint32_t hi = pack_round<T>(weight_of(sc[h][2], mref), weight_of(sc[h][3], mref), pr[2], pr[3]);
-          pa[h] = lo;      // a0 (row g) / a1 (row g+8): tokens 2t, 2t+1
-          pa[h + 2] = hi;  // a2 / a3: tokens 8+2t, 8+2t+1
-          const float psum = __fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3]));
-          l_r[h] = __fadd_rn(__fmul_rn(l_r[h], alpha[h]), psum);
-          m_r[h] = m_new;
-        }
-        if (alpha[0] != 1.0f || alpha[1] != 1.0f) {   // multiplying by exactly 1 changes nothing
-#pragma unroll
-          for (int j = 0; j < NT; ++j) {
-            o[j][0] = __fmul_rn(o[j][0], alpha[0]);
-            o[j][1] = __fmul_rn(o[j][1], alpha[0]);
-            o[j][2] = __fmul_rn(o[j][2], alpha[1]);
-            o[j][3] = __fmul_rn(o[j][3], alpha[1]);
+          for (int kc = 0; kc < KC; ++kc) {
+            uint32_t ka[4];
+            ldsm_x4(kbase + k_off[kc], ka[0], ka[1], ka[2], ka[3]);
+            mma16816<T>(st, ka, qa[kc][0], qa[kc][1]);
           }
-        }
-        // O += P V
+          const int tk = t0 + g;
+          float x0 = __fmul_rn(st[0], p.scale_log2);
+          float x1 = __fmul_rn(st[2], p.scale_log2);
+          if (t4 != 0 || tk >= end_t1) x0 = -INFINITY;
+          if (t4 != 0 || tk + 8 >= end_t1) x1 = -INFINITY;
+          float mx = fmaxf(x0, x1);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          mx = __shfl_sync(0xffffffffu, mx, 0);   // the row's max on every lane (lanes t4 != 0 hold -inf)
+          const float m_new = fmaxf(m_r[0], mx);
+          const float mref = (m_new == -INFINITY) ? 0.0f : m_new;
+          const float alpha = weight_of(m_r[0], mref);
+          float r0f, r1f;
+          const uint32_t pk = pack_round<T>(weight_of(x0, mref), weight_of(x1, mref), r0f, r1f);   // tokens g | g+8
+          // P^T as the B operand: lane t4 of column 0 takes tokens 2t4, 2t4+1 (b0) and
+          // 2t4+8, 2t4+9 (b1) from lanes 8*t4 and 8*t4+4
+          const uint32_t ua = __shfl_sync(0xffffffffu, pk, 8 * t4);
+          const uint32_t ub = __shfl_sync(0xffffffffu, pk, 8 * t4 + 4);
+          uint32_t pb0 = __byte_perm(ua, ub, 0x5410);
+          uint32_t pb1 = __byte_perm(ua, ub, 0x7632);
+          if (g != 0) pb0 = pb1 = 0u;
+          // l from the same four tokens per lane and in the same order as the 16-row form
+          const float psum =
+              __fadd_rn(__fadd_rn(lo_f32<T>(pb0), hi_f32<T>(pb0)), __fadd_rn(lo_f32<T>(pb1), hi_f32<T>(pb1)));
+          l_r[0] = __fadd_rn(__fmul_rn(l_r[0], alpha), psum);
+          m_r[0] = m_new;
+          if (alpha != 1.0f) {   // multiplying by exactly 1 changes nothing
 #pragma unroll
-        for (int pc = 0; pc < D / 16; ++pc) {
-          uint32_t b0a, b1a, b0b, b1b;
-          ldsm_x4_t(vbase + v_off[pc], b0a, b1a, b0b, b1b);
-          mma16816<T>(o[2 * pc], pa, b0a, b1a);
-          mma16816<T>(o[2 * pc + 1], pa, b0b, b1b);
+            for (int j = 0; j < NO; ++j) {
+              o[j][0] = __fmul_rn(o[j][0], alpha);
+              o[j][2] = __fmul_rn(o[j][2], alpha);
+            }
+          }
+          // O^T += V^T P^T
+#pragma unroll
+          for (int pc = 0; pc < D / 16; ++pc) {
+            uint32_t va[4];
+            ldsm_x4_t(vbase + v_off[pc], va[0], va[1], va[2], va[3]);
+            mma16816<T>(o[pc], va, pb0, pb1);
+          }
+        } else {
+          // S = Q K^T for this warp's 16 tokens (two n-tiles of 8 tokens).
+          float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+  #pragma unroll
+          for (int kc = 0; kc < KC; ++kc) {
+            uint32_t b00, b01, b10, b11;
+            ldsm_x4(kbase + k_off[kc], b00, b01, b10, b11);
+            mma16816<T>(s0, qa[kc], b00, b01);
+            mma16816<T>(s1, qa[kc], b10, b11);
+          }
+
+          // scale, mask, online softmax update (rows rho0 -> s*[0..1], rho1 -> s*[2..3])
+          const int tk = t0 + 2 * t4;
+          float sc[2][4];
+          sc[0][0] = __fmul_rn(s0[0], p.scale_log2);
+          sc[0][1] = __fmul_rn(s0[1], p.scale_log2);
+          sc[0][2] = __fmul_rn(s1[0], p.scale_log2);
+          sc[0][3] = __fmul_rn(s1[1], p.scale_log2);
+          sc[1][0] = __fmul_rn(s0[2], p.scale_log2);
+          sc[1][1] = __fmul_rn(s0[3], p.scale_log2);
+          sc[1][2] = __fmul_rn(s1[2], p.scale_log2);
+          sc[1][3] = __fmul_rn(s1[3], p.scale_log2);
+          if (tk + 9 >= end0 || tk + 9 >= end1) {   // some of this thread's tokens are past a row's end
+            if (tk + 0 >= end0) sc[0][0] = -INFINITY;
+            if (tk + 1 >= end0) sc[0][1] = -INFINITY;
+            if (tk + 8 >= end0) sc[0][2] = -INFINITY;
+            if (tk + 9 >= end0) sc[0][3] = -INFINITY;
+            if (tk + 0 >= end1) sc[1][0] = -INFINITY;
+            if (tk + 1 >= end1) sc[1][1] = -INFINITY;
+            if (tk + 8 >= end1) sc[1][2] = -INFINITY;
+            if (tk + 9 >= end1) sc[1][3] = -INFINITY;
+          }
+
+          uint32_t pa[4];
+          float alpha[2];
+  #pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float mx = fmaxf(fmaxf(sc[h][0], sc[h][1]), fmaxf(sc[h][2], sc[h][3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float m_new = fmaxf(m_r[h], mx);
+            const float mref = (m_new == -INFINITY) ? 0.0f : m_new;
+            alpha[h] = weight_of(m_r[h], mref);
+            float pr[4];
+            const uint32_t lo = pack_round<T>(weight_of(sc[h][0], mref), weight_of(sc[h][1], mref), pr[0], pr[1]);
+            const uint32_t hi = pack_round<T>(weight_of(sc[h][2], mref), weight_of(sc[h][3], mref), pr[2], pr[3]);
+            pa[h] = lo;      // a0 (row g) / a1 (row g+8): tokens 2t, 2t+1
+            pa[h + 2] = hi;  // a2 / a3: tokens 8+2t, 8+2t+1
+            const float psum = __fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3]));
+            l_r[h] = __fadd_rn(__fmul_rn(l_r[h], alpha[h]), psum);
+            m_r[h] = m_new;
+          }
+          if (alpha[0] != 1.0f || alpha[1] != 1.0f) {   // multiplying by exactly 1 changes nothing
+  #pragma unroll
+            for (int j = 0; j < NT; ++j) {
+              o[j][0] = __fmul_rn(o[j][0], alpha[0]);
+              o[j][1] = __fmul_rn(o[j][1], alpha[0]);
+              o[j][2] = __fmul_rn(o[j][2], alpha[1]);
+              o[j][3] = __fmul_rn(o[j][3], alpha[1]);
+            }
+          }
+          // O += P V
+  #pragma unroll
+          for (int pc = 0; pc < D / 16; ++pc) {
+            uint32_t b0a, b1a, b0b, b1b;
+            ldsm_x4_t(vbase + v_off[pc], b0a, b1a, b0b, b1b);
+            mma16816<T>(o[2 * pc], pa, b0a, b1a);
+            mma16816<T>(o[2 * pc + 1], pa, b0b, b1b);
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[stage]);
@@ -580,14 +673,26 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
 
       // quad-reduce l (fixed butterfly; m is already quad-uniform)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < (T1 ? 1 : 2); ++h) {
         l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 1));
         l_r[h] = __fadd_rn(l_r[h], __shfl_xor_sync(0xffffffffu, l_r[h], 2));
       }
 
       // ---- merge the four warps of this split in warp order ----
       if (!csync(cbar, cphase, abort_flag)) break;   // the previous split's merge reads are done
-      if (v0) {
+      if constexpr (T1) {
+        if (t4 == 0) {
+#pragma unroll
+          for (int j = 0; j < NO; ++j) {
+            comb_o[warp * C::CSTRIDE + j * 16 + g] = o[j][0];
+            comb_o[warp * C::CSTRIDE + j * 16 + g + 8] = o[j][2];
+          }
+        }
+        if (lane == 0) {
+          comb_ml[warp * 2 + 0] = m_r[0];
+          comb_ml[warp * 2 + 1] = l_r[0];
+        }
+      } else if (v0) {
 #pragma unroll
         for (int j = 0; j < NT; ++j)
           *reinterpret_cast<float2*>(comb_o + (warp * p.rows_cap + rho0) * C::CSTRIDE + j * 8 + 2 * t4) =
@@ -597,7 +702,7 @@ __global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
           comb_ml[(warp * p.rows_cap + rho0) * 2 + 1] = l_r[0];
         }
       }
-      if (v1) {
+      if (!T1 && v1) {
 #pragma unroll
         for (int j = 0; j < NT; ++j)
           *reinterpret_cast<float2*>(comb_o + (warp * p.rows_cap + rho1) * C::CSTRIDE + j * 8 + 2 * t4) =

@@ -382,13 +382,13 @@ AttnPlan plan_attention(int32_t n_tiles, int32_t rows_per_tile, int32_t hq, int3
   return pl;
 }
 
-template <typename T, int D, int KM>
+template <typename T, int D, int KM, bool T1>
 int attn_launch_km(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int64_t n_items,
                    cudaStream_t st) {
   using C = dk::attn::Cfg<D>;
   static bool done[kMaxDevices] = {false};
   static int resident[kMaxDevices][dk::attn::kRows + 1] = {};   // CTAs per SM, by rows_cap
-  auto fn = dk::attn::attn_kernel<T, D, KM>;
+  auto fn = dk::attn::attn_kernel<T, D, KM, T1>;
   int rc = ensure_smem(fn, C::smem_bytes(dk::attn::kRows), done);
   if (rc) return rc;
   const int dev = current_device();
@@ -417,8 +417,9 @@ int attn_launch(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Pa
                 cudaStream_t st) {
   constexpr int kThr = dk::attn::kConsumerWarps * 32;
   constexpr int kNarrow = (4 < dk::attn::Cfg<D>::KMAX) ? 4 : dk::attn::Cfg<D>::KMAX;
-  if (p.rows_cap * D <= kNarrow * kThr) return attn_launch_km<T, D, kNarrow>(tk, tv, p, n_items, st);
-  return attn_launch_km<T, D, dk::attn::Cfg<D>::KMAX>(tk, tv, p, n_items, st);
+  if (p.rows_cap == 1) return attn_launch_km<T, D, 1, true>(tk, tv, p, n_items, st);
+  if (p.rows_cap * D <= kNarrow * kThr) return attn_launch_km<T, D, kNarrow, false>(tk, tv, p, n_items, st);
+  return attn_launch_km<T, D, dk::attn::Cfg<D>::KMAX, false>(tk, tv, p, n_items, st);
 }
 
 template <typename T, int DK, int DV>
@@ -527,8 +528,8 @@ int dk_kernel_attributes(int which, int* num_regs, int* max_threads, int* local_
   cudaError_t e;
   switch (which) {
     case 0: e = cudaFuncGetAttributes(&a, dk::gemm::gemm_kernel<__nv_bfloat16, 1, true>); break;
-    case 1: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 128, 4>); break;
-    case 2: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 64, 4>); break;
+    case 1: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 128, 4, false>); break;
+    case 2: e = cudaFuncGetAttributes(&a, dk::attn::attn_kernel<__nv_bfloat16, 64, 4, false>); break;
     case 3: e = cudaFuncGetAttributes(&a, dk::rmsnorm_inv_vec_kernel<float, float, 8>); break;
     default: return fail(DK_ERR_INVALID_ARGUMENT, "dk_kernel_attributes: unknown kernel %d", which);
   }
