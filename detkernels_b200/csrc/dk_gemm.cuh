@@ -131,6 +131,21 @@ enum : int {
   kDetDrain = 0x105,
 };
 
+// Output tile t -> (m-tile, n-tile).  Tiles go in bands of kBandM m-tiles; inside a
+// band the m-tile varies fastest, then the n-tile.  The ~SM-count tiles in flight at
+// once then share a few activation and weight tiles in L2, and a tall activation
+// matrix streams from DRAM about once per GEMM instead of once per n-tile.  This is
+// order only: a tile's arithmetic does not depend on when or where it runs.
+constexpr int kBandM = 16;
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& mt, int& nt) {
+  const int per_band = kBandM * p.n_tiles;
+  const int band = t / per_band;
+  const int r = t - band * per_band;
+  const int bm = min(kBandM, p.m_tiles - band * kBandM);
+  nt = r / bm;
+  mt = band * kBandM + (r - nt * bm);
+}
+
 __device__ __forceinline__ void slice_bounds(const Params& p, int s, int& k0, int& k1) {
   k0 = s * p.slice_len;
   k1 = min(k0 + p.slice_len, p.K);
@@ -491,8 +506,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x) {
         const int g = u % n_groups;
         const int t = u / n_groups;
-        const int mt = t % p.m_tiles;
-        const int nt = t / p.m_tiles;
+        int mt, nt;
+        tile_coords(p, t, mt, nt);
         for (int si = 0; si < p.group && !abort_flag; ++si) {
           const int s = p.slice_begin + g * p.group + si;
           int k0, k1;
@@ -592,8 +607,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++ordinal) {
       const int g = u % n_groups;
       const int t = u / n_groups;
-      const int mt = t % p.m_tiles;
-      const int nt = t / p.m_tiles;
+      int mt, nt;
+      tile_coords(p, t, mt, nt);
       const int n = nt * kTileN + n_local;
       const int m0 = mt * kTileM + col0;
       const bool n_ok = n < p.N;
@@ -690,6 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename T>
 __global__ void __launch_bounds__(256) fold_groups_kernel(const float* __restrict__ partials, int n_parts, const Params p) {
   pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
   const int M = p.M, N = p.N;
   T* c = static_cast<T*>(p.c);
   const int64_t MN = static_cast<int64_t>(M) * N;
@@ -755,6 +771,7 @@ __global__ void __launch_bounds__(256) fold_groups_kernel(const float* __restric
 __global__ void argmax_finish_kernel(unsigned long long* __restrict__ keys, int64_t n_rows, int64_t* tokens,
                                      int64_t* tokens_copy, int32_t* lens_a, int32_t* lens_b) {
   pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
   for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < n_rows;
        r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const unsigned long long k = keys[r];

@@ -146,15 +146,17 @@ int rmsnorm_inv_launch(const void* x, int64_t xs, const void* w, void* y, int64_
   constexpr int VEC = dk::Vec16<T>::N;
   const bool vec = (cols % VEC == 0) && (xs % VEC == 0) && (ys % VEC == 0) && aligned16(x) && aligned16(y);
   const dim3 grid(static_cast<unsigned>(rows));
+  cudaError_t e;
   if (vec) {
     constexpr int MAXC = (sizeof(T) == 4) ? 8 : 4;
-    dk::rmsnorm_inv_vec_kernel<T, W, MAXC><<<grid, dk::kRmsThreads, 0, st>>>(
-        static_cast<const T*>(x), xs, static_cast<const W*>(w), static_cast<T*>(y), ys, cols, eps);
+    e = launch_pdl(dk::rmsnorm_inv_vec_kernel<T, W, MAXC>, grid, dim3(dk::kRmsThreads), 0, st,
+                   static_cast<const T*>(x), xs, static_cast<const W*>(w), static_cast<T*>(y), ys, cols, eps);
   } else {
-    dk::rmsnorm_inv_scalar_kernel<T, W><<<grid, dk::kRmsThreads, 0, st>>>(
-        static_cast<const T*>(x), xs, static_cast<const W*>(w), static_cast<T*>(y), ys, cols, eps);
+    e = launch_pdl(dk::rmsnorm_inv_scalar_kernel<T, W>, grid, dim3(dk::kRmsThreads), 0, st,
+                   static_cast<const T*>(x), xs, static_cast<const W*>(w), static_cast<T*>(y), ys, cols, eps);
   }
-  return check_launch("rmsnorm_batch_invariant");
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "rmsnorm_batch_invariant: launch failed: %s", cudaGetErrorString(e));
+  return DK_OK;
 }
 
 template <typename T, typename W>
@@ -281,7 +283,10 @@ template <typename T>
 int launch_fold(const float* partials, int n_parts, const dk::gemm::Params& p, cudaStream_t st) {
   const int64_t total = static_cast<int64_t>(p.M) * ceil_div(p.N, 4);
   const int64_t want = ceil_div(total, 256);
-  const int blocks = static_cast<int>(want < 8 * 148 ? want : 8 * 148);
+  // one resident wave (4 blocks per SM), so every block has issued the early
+  // dependent-launch trigger soon after the GEMM completes
+  const int64_t cap = 4 * static_cast<int64_t>(sm_count(current_device()));
+  const int blocks = static_cast<int>(want < cap ? want : cap);
   cudaError_t e = launch_pdl(dk::gemm::fold_groups_kernel<T>, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, st,
                              partials, n_parts, p);
   if (e != cudaSuccess) return fail(DK_ERR_CUDA, "matmul fold: launch failed: %s", cudaGetErrorString(e));

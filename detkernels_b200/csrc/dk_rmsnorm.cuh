@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_inv_vec_kernel(const T* _
                                                                        const W* __restrict__ w,
                                                                        T* __restrict__ y, int64_t ys,
                                                                        int64_t n_cols, float eps) {
+  pdl_wait();   // x may come from the previous kernel
+  if (threadIdx.x == 0) pdl_launch_dependents();
   constexpr int VEC = Vec16<T>::N;
   __shared__ float red[9];
   const int64_t row = blockIdx.x;
@@ -119,6 +121,8 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_inv_scalar_kernel(const T
                                                                           const W* __restrict__ w,
                                                                           T* __restrict__ y, int64_t ys,
                                                                           int64_t n_cols, float eps) {
+  pdl_wait();   // x may come from the previous kernel
+  if (threadIdx.x == 0) pdl_launch_dependents();
   constexpr int VEC = Vec16<T>::N;
   __shared__ float red[9];
   const int64_t row = blockIdx.x;
