@@ -87,6 +87,7 @@ DK_EPI_SILU = 2
 DK_EPI_SILU_MUL = 3
 DK_EPI_QKV_CACHE = 4
 DK_EPI_ARGMAX = 5
+DK_EPI_RESIDUAL_RMSNORM = 6
 
 
 class MatmulEpilogue(ctypes.Structure):
@@ -96,7 +97,8 @@ class MatmulEpilogue(ctypes.Structure):
                 ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
                 ("cache_stride_seq", ctypes.c_int64), ("cache_stride_head", ctypes.c_int64),
                 ("cache_stride_tok", ctypes.c_int64), ("row_seq", ctypes.c_void_p), ("row_pos", ctypes.c_void_p),
-                ("argmax_keys", ctypes.c_void_p)]
+                ("argmax_keys", ctypes.c_void_p), ("norm_w", ctypes.c_void_p), ("norm_w_dtype", ctypes.c_int),
+                ("norm_out", ctypes.c_void_p), ("norm_ld", ctypes.c_int64), ("norm_eps", ctypes.c_float)]
 
 
 class DetKernelsError(RuntimeError):

@@ -50,6 +50,7 @@
 #pragma once
 
 #include "dk_common.cuh"
+#include "dk_rmsnorm.cuh"
 
 namespace dk {
 namespace gemm {
@@ -763,6 +764,91 @@ __global__ void __launch_bounds__(256) fold_groups_kernel(const float* __restric
 #pragma unroll
       for (int e = 0; e < 4; ++e)
         if (n0 + e < N) store_final<T>(p, c, static_cast<int>(m), n0 + e, fin[e]);
+    }
+  }
+}
+
+// Four consecutive columns n0 .. n0+3 (n0 a multiple of 4) of row m of partial j of
+// [n_parts][M][N] f32; vec: N % 4 == 0 (one 16-byte load).
+__device__ __forceinline__ float4 load_quad(const float* __restrict__ partials, int j, int64_t MN, int N, int64_t m,
+                                            int n0, bool vec) {
+  const float* src = partials + j * MN + m * N + n0;
+  if (vec) return __ldcg(reinterpret_cast<const float4*>(src));
+  float4 q;
+  q.x = __ldcg(src);
+  q.y = (n0 + 1 < N) ? __ldcg(src + 1) : 0.0f;
+  q.z = (n0 + 2 < N) ? __ldcg(src + 2) : 0.0f;
+  q.w = (n0 + 3 < N) ? __ldcg(src + 3) : 0.0f;
+  return q;
+}
+
+// DK_EPI_RESIDUAL_RMSNORM after a SPLIT launch: one CTA of kRmsThreads per row m.
+// h[m, :] = round(R[m, :] + round(upper tree levels over the partials)) is stored to C,
+// then y[m, :] = RMSNorm(h[m, :]) * w -- with the invariant RMSNorm kernel's chunk
+// ownership (thread t: 16-byte chunks t, t + 256, ...), its x^2 accumulation order and
+// its butterflies, so h and y carry the bits of the fold kernel followed by that kernel.
+// Needs N % VEC == 0, N <= MAXC * 256 * VEC and 16-byte aligned rows of C and y.
+template <typename T, typename W, int MAXC>
+__global__ void __launch_bounds__(kRmsThreads) fold_residual_rmsnorm_kernel(const float* __restrict__ partials,
+                                                                            int n_parts, const Params p,
+                                                                            const W* __restrict__ w, T* y,
+                                                                            int64_t ldy, float eps) {
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  constexpr int VEC = Vec16<T>::N;
+  __shared__ float red[9];
+  const int64_t m = blockIdx.x;
+  const int N = p.N;
+  const int64_t MN = static_cast<int64_t>(p.M) * N;
+  const int nchunks = N / VEC;
+  const T* R = static_cast<const T*>(p.epi.resid) + m * p.epi.ld_resid;
+  T* hr = static_cast<T*>(p.c) + m * p.ldc;
+  Vec16<T> keep[MAXC];
+  float acc = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = threadIdx.x + i * kRmsThreads;
+    if (c < nchunks) {
+#pragma unroll
+      for (int q = 0; q < VEC / 4; ++q) {
+        const int n0 = c * VEC + 4 * q;
+        float4 v[kSlices];
+#pragma unroll
+        for (int j = 0; j < kSlices; ++j)
+          v[j] = (j < n_parts) ? load_quad(partials, j, MN, N, m, n0, true) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float col[kSlices];
+#pragma unroll
+          for (int j = 0; j < kSlices; ++j) col[j] = e == 0 ? v[j].x : (e == 1 ? v[j].y : (e == 2 ? v[j].z : v[j].w));
+          const float fin = tree_sum(col, n_parts);
+          // the residual element is read before this thread overwrites it (R may be C)
+          keep[i].v[4 * q + e] = from_f32<T>(__fadd_rn(to_f32<T>(R[n0 + e]), rnd<T>(fin)));
+        }
+      }
+      *reinterpret_cast<Vec16<T>*>(hr + c * VEC) = keep[i];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float f = to_f32<T>(keep[i].v[j]);
+        acc = __fmaf_rn(f, f, acc);
+      }
+    }
+  }
+  const float total = block_sum_256(acc, red);
+  const float var = __fdiv_rn(total, static_cast<float>(N));
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  T* yr = y + m * ldy;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = threadIdx.x + i * kRmsThreads;
+    if (c < nchunks) {
+      Vec16<T> o;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float xn = __fmul_rn(to_f32<T>(keep[i].v[j]), rstd);
+        o.v[j] = from_f32<T>(__fmul_rn(xn, to_f32<W>(w[c * VEC + j])));
+      }
+      *reinterpret_cast<Vec16<T>*>(yr + c * VEC) = o;
     }
   }
 }

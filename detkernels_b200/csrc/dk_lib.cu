@@ -293,8 +293,49 @@ int launch_fold(const float* partials, int n_parts, const dk::gemm::Params& p, c
   return DK_OK;
 }
 
+// The RMSNorm half of DK_EPI_RESIDUAL_RMSNORM (the GEMM itself runs DK_EPI_RESIDUAL).
+struct NormSpec {
+  const void* w;
+  int w_dtype;
+  void* out;
+  int64_t ld;
+  float eps;
+};
+
+template <typename T, typename W>
+int launch_fold_rmsnorm_t(const float* partials, int n_parts, const dk::gemm::Params& p, const NormSpec& nm,
+                          cudaStream_t st) {
+  cudaError_t e = launch_pdl(dk::gemm::fold_residual_rmsnorm_kernel<T, W, 4>, dim3(static_cast<unsigned>(p.M)),
+                             dim3(dk::kRmsThreads), 0, st, partials, n_parts, p, static_cast<const W*>(nm.w),
+                             static_cast<T*>(nm.out), nm.ld, nm.eps);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "matmul fold+rmsnorm: launch failed: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
+
+// Upper tree levels + residual + RMSNorm in one kernel when a CTA can hold a row in
+// 16-byte chunks; otherwise the fold kernel followed by the RMSNorm kernel (same bits).
+int launch_fold_norm(int dtype, const float* partials, int n_parts, const dk::gemm::Params& p, const NormSpec& nm,
+                     cudaStream_t st) {
+  constexpr int kVec = 8;   // 16-bit elements per 16-byte chunk
+  const bool fused = (p.N % kVec == 0) && (p.N <= 4 * dk::kRmsThreads * kVec) && (p.ldc % kVec == 0) &&
+                     (nm.ld % kVec == 0) && aligned16(p.c) && aligned16(nm.out) &&
+                     (nm.w_dtype == dtype || nm.w_dtype == DK_F32);
+  if (fused) {
+    if (dtype == DK_BF16) {
+      if (nm.w_dtype == DK_F32) return launch_fold_rmsnorm_t<__nv_bfloat16, float>(partials, n_parts, p, nm, st);
+      return launch_fold_rmsnorm_t<__nv_bfloat16, __nv_bfloat16>(partials, n_parts, p, nm, st);
+    }
+    if (nm.w_dtype == DK_F32) return launch_fold_rmsnorm_t<__half, float>(partials, n_parts, p, nm, st);
+    return launch_fold_rmsnorm_t<__half, __half>(partials, n_parts, p, nm, st);
+  }
+  int rc = (dtype == DK_BF16) ? launch_fold<__nv_bfloat16>(partials, n_parts, p, st)
+                              : launch_fold<__half>(partials, n_parts, p, st);
+  if (rc) return rc;
+  return dk_rmsnorm_batch_invariant(p.c, p.ldc, nm.w, nm.out, nm.ld, p.M, p.N, dtype, nm.w_dtype, nm.eps, st);
+}
+
 int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb, dk::gemm::Params p,
-                cudaStream_t st, const char* what) {
+                cudaStream_t st, const char* what, const NormSpec* norm = nullptr) {
   p.a_rows = (p.m_tiles == 1) ? static_cast<int>(ceil_div(p.M, 8) * 8) : dk::gemm::kTileM;
   const int64_t k_mem = p.k_extent > 0 ? p.k_extent : p.K;
   CUtensorMap tmB, tmA;
@@ -332,8 +373,15 @@ int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ld
   if (p.mode == dk::gemm::SPLIT) {
     // the upper tree levels over the groups' subtree sums, as a dependent launch
     const int n_parts = (p.slice_end - p.slice_begin) / p.group;
+    if (norm) return launch_fold_norm(dtype, p.ws, n_parts, p, *norm, st);
     if (dtype == DK_BF16) return launch_fold<__nv_bfloat16>(p.ws, n_parts, p, st);
     return launch_fold<__half>(p.ws, n_parts, p, st);
+  }
+  if (norm) {
+    const int rc = check_launch(what);
+    if (rc) return rc;
+    return dk_rmsnorm_batch_invariant(p.c, p.ldc, norm->w, norm->out, norm->ld, p.M, p.N, dtype, norm->w_dtype,
+                                      norm->eps, st);
   }
   return check_launch(what);
 }
@@ -626,6 +674,11 @@ int dk_matmul_batch_invariant_ex(const void* a, int64_t lda, const void* b, int6
     case DK_EPI_RESIDUAL:
       if (!e.resid || e.ld_resid < N) return fail(DK_ERR_INVALID_ARGUMENT, "%s: residual epilogue needs R", what);
       break;
+    case DK_EPI_RESIDUAL_RMSNORM:
+      if (!e.resid || e.ld_resid < N) return fail(DK_ERR_INVALID_ARGUMENT, "%s: residual epilogue needs R", what);
+      if (!e.norm_w || !e.norm_out || e.norm_ld < N || !valid_dtype(e.norm_w_dtype))
+        return fail(DK_ERR_INVALID_ARGUMENT, "%s: RMSNorm epilogue needs a weight, an output and norm_ld >= N", what);
+      break;
     case DK_EPI_SILU_MUL:
       if (N % 2) return fail(DK_ERR_INVALID_ARGUMENT, "%s: gate/up epilogue needs an even N", what);
       out_cols = N / 2;
@@ -672,6 +725,11 @@ int dk_matmul_batch_invariant_ex(const void* a, int64_t lda, const void* b, int6
                   workspace_bytes);
     if (!aligned16(workspace)) return fail(DK_ERR_WORKSPACE, "%s: workspace must be 16-byte aligned", what);
     p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.partials_off);
+  }
+  if (e.mode == DK_EPI_RESIDUAL_RMSNORM) {
+    const NormSpec nm{e.norm_w, e.norm_w_dtype, e.norm_out, e.norm_ld, e.norm_eps};
+    p.epi.mode = DK_EPI_RESIDUAL;   // the GEMM (or its fold) writes C; the norm follows from it
+    return gemm_launch(dtype, a, lda, b, ldb, p, st, what, &nm);
   }
   return gemm_launch(dtype, a, lda, b, ldb, p, st, what);
 }

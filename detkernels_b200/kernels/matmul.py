@@ -147,11 +147,13 @@ def matmul_fold_slices(partials, dtype, out=None):
 
 
 _EPILOGUES = {"store": _lib.DK_EPI_STORE, "residual": _lib.DK_EPI_RESIDUAL, "silu": _lib.DK_EPI_SILU,
-              "silu_mul": _lib.DK_EPI_SILU_MUL, "qkv_cache": _lib.DK_EPI_QKV_CACHE, "argmax": _lib.DK_EPI_ARGMAX}
+              "silu_mul": _lib.DK_EPI_SILU_MUL, "qkv_cache": _lib.DK_EPI_QKV_CACHE, "argmax": _lib.DK_EPI_ARGMAX,
+              "residual_rmsnorm": _lib.DK_EPI_RESIDUAL_RMSNORM}
 
 
 def matmul_fused(a, b, epilogue: str = "store", out=None, workspace=None, residual=None, q_cols: int = 0,
-                 head_dim: int = 0, k_cache=None, v_cache=None, row_seq=None, row_pos=None, argmax_keys=None):
+                 head_dim: int = 0, k_cache=None, v_cache=None, row_seq=None, row_pos=None, argmax_keys=None,
+                 norm_weight=None, norm_out=None, eps: float = 1e-6):
     """``matmul_batch_invariant`` (same K numerics) with the decoder's next element-wise op fused
     into the store; every step rounds where the unfused torch sequence rounds, so the result bits
     equal that sequence's.  Epilogues:
@@ -167,6 +169,9 @@ def matmul_fused(a, b, epilogue: str = "store", out=None, workspace=None, residu
     * ``"argmax"``: folds each row's first maximal column into ``argmax_keys`` (int64 [M] used as
       uint64, zero before the call; ``argmax_finish`` reads and re-zeroes them).  Logits are stored
       only when ``out`` is given.
+    * ``"residual_rmsnorm"``: ``"residual"``, and ``norm_out`` ([M, N]) receives
+      ``rmsnorm_batch_invariant(result, norm_weight, eps)`` -- the bits of the two calls, with the
+      norm computed while the split-K sums are folded.
     """
     import ctypes
 
@@ -178,10 +183,17 @@ def matmul_fused(a, b, epilogue: str = "store", out=None, workspace=None, residu
     epi = _lib.MatmulEpilogue()
     epi.mode = _EPILOGUES[epilogue]
     out_cols = N
-    if epilogue == "residual":
+    if epilogue in ("residual", "residual_rmsnorm"):
         assert residual is not None and residual.shape == (M, N) and residual.dtype == a.dtype
         assert residual.is_cuda and residual.stride(1) == 1
         epi.resid, epi.ld_resid = residual.data_ptr(), residual.stride(0)
+        if epilogue == "residual_rmsnorm":
+            assert norm_weight is not None and norm_weight.is_cuda and norm_weight.is_contiguous()
+            assert norm_weight.numel() == N
+            assert norm_out is not None and norm_out.shape == (M, N) and norm_out.dtype == a.dtype
+            assert norm_out.stride(1) == 1
+            epi.norm_w, epi.norm_w_dtype = norm_weight.data_ptr(), _lib.dtype_code(norm_weight.dtype)
+            epi.norm_out, epi.norm_ld, epi.norm_eps = norm_out.data_ptr(), norm_out.stride(0), float(eps)
     elif epilogue == "silu_mul":
         if N % 2:
             raise ValueError("silu_mul needs an even number of columns")

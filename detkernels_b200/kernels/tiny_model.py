@@ -293,14 +293,20 @@ class DecodeEngine:
     def _mm(self, x, w, epilogue="store", **kw):
         return matmul_fused(x, w, epilogue, workspace=self.gemm_ws, **kw)
 
-    def _layer(self, li, layer, x, write_seq, write_pos, q_lens, row_tiles, max_len, attn_ws, events=None):
-        """One transformer block over R rows.  The QKV matmul writes K/V of every row
-        to (write_seq, write_pos) (int32; write_seq None: row r is sequence r) before
-        attention reads them."""
+    def _next_norm_w(self, li):
+        """The RMSNorm weight applied to block li's output: block li+1's input norm, or the final norm."""
+        return self.layers[li + 1]["norm1_w"] if li + 1 < len(self.layers) else self.model.norm_f_w
+
+    def _layer(self, li, layer, x, xn, write_seq, write_pos, q_lens, row_tiles, max_len, attn_ws, events=None):
+        """One transformer block over R rows; xn = rmsnorm(x, norm1_w).  Returns (x', xn') with
+        xn' = x' under the next norm (block li+1's input norm or the final norm), computed by the
+        down projection's epilogue.  The QKV matmul writes K/V of every row to (write_seq,
+        write_pos) (int32; write_seq None: row r is sequence r) before attention reads them."""
+        import torch
+
         cfg = self.cfg
         R = x.shape[0]
         H, D = self.H, self.D
-        xn = rmsnorm_batch_invariant(x, layer["norm1_w"], cfg.eps)
         q = self._mm(xn, layer["w_qkv"], "qkv_cache", q_cols=H * D, head_dim=D, k_cache=self.k_cache[li],
                      v_cache=self.v_cache[li], row_seq=write_seq, row_pos=write_pos)
         if events is not None:
@@ -309,16 +315,20 @@ class DecodeEngine:
                                 max_kv_len=max_len, workspace=attn_ws)
         if events is not None:
             events[1].record()
-        x = self._mm(attn.reshape(R, H * D), layer["w_o"], "residual", residual=x)
-        xn = rmsnorm_batch_invariant(x, layer["norm2_w"], cfg.eps)
+        xn = torch.empty_like(x)
+        x = self._mm(attn.reshape(R, H * D), layer["w_o"], "residual_rmsnorm", residual=x,
+                     norm_weight=layer["norm2_w"], norm_out=xn, eps=cfg.eps)
         if cfg.mlp == "swiglu":
             hid = self._mm(xn, layer["w_gu"], "silu_mul")
         else:
             hid = self._mm(xn, layer["w_mlp1"], "silu")
-        return self._mm(hid, layer["w_mlp2"], "residual", residual=x)
+        xn_next = torch.empty_like(x)
+        x = self._mm(hid, layer["w_mlp2"], "residual_rmsnorm", residual=x, norm_weight=self._next_norm_w(li),
+                     norm_out=xn_next, eps=cfg.eps)
+        return x, xn_next
 
-    def _logits(self, x):
-        xn = rmsnorm_batch_invariant(x, self.model.norm_f_w, self.cfg.eps)
+    def _logits(self, xn):
+        """Logits of rows already under the final norm."""
         return self._mm(xn, self.model.w_lm_head)
 
     # ---------------- prefill ----------------
@@ -377,10 +387,11 @@ class DecodeEngine:
         self.gemm_ws = plan["gemm_ws"]
         try:
             x = self.model.embed[plan["tok"]]
+            xn = rmsnorm_batch_invariant(x, self.layers[0]["norm1_w"], self.cfg.eps)
             for li, layer in enumerate(self.layers):
-                x = self._layer(li, layer, x, plan["rows32"], plan["pos32"], plan["q_lens"], plan["tiles"],
-                                plan["max_len"], plan["attn_ws"])
-            logits = self._logits(x[plan["last"]])
+                x, xn = self._layer(li, layer, x, xn, plan["rows32"], plan["pos32"], plan["q_lens"], plan["tiles"],
+                                    plan["max_len"], plan["attn_ws"])
+            logits = self._logits(xn[plan["last"]])
         finally:
             self.gemm_ws = saved
         self.kv_lens.zero_()
@@ -396,14 +407,14 @@ class DecodeEngine:
         import torch
 
         x = self.model.embed[self.tokens]
+        xn = rmsnorm_batch_invariant(x, self.layers[0]["norm1_w"], self.cfg.eps)
         for li, layer in enumerate(self.layers):
             ev = None
             if events is not None:
                 ev = (torch.cuda.Event(enable_timing=True, external=True),
                       torch.cuda.Event(enable_timing=True, external=True))
                 events.append(ev)
-            x = self._layer(li, layer, x, None, self.kv_lens, self.q_lens, None, max_len, self.attn_ws, ev)
-        xn = rmsnorm_batch_invariant(x, self.model.norm_f_w, self.cfg.eps)
+            x, xn = self._layer(li, layer, x, xn, None, self.kv_lens, self.q_lens, None, max_len, self.attn_ws, ev)
         self._mm(xn, self.model.w_lm_head, "argmax", argmax_keys=self.argmax_keys)
         argmax_finish(self.argmax_keys, self.tokens, out_row, self.kv_lens, self.q_lens)
         return self.tokens

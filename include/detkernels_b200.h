@@ -147,6 +147,9 @@ int dk_matmul_batch_variant(const void* a, int64_t lda, const void* b, int64_t l
                               (ordered value << 32 | ~n): order-free, so deterministic.  C is optional
                               (NULL: logits are not stored).  argmax_keys must be 0 before the call;
                               dk_argmax_finish reads and re-zeroes them. */
+#define DK_EPI_RESIDUAL_RMSNORM 6 /* C = round(R + round(v)) as DK_EPI_RESIDUAL, then norm_out[m, :] =
+                                 * dk_rmsnorm_batch_invariant(C[m, :], norm_w, eps): the same bits as the two
+                                 * calls, with the norm computed while C is folded (one launch fewer) */
 typedef struct dk_matmul_epilogue {
   int mode;
   const void* resid;       /* DK_EPI_RESIDUAL: R, same dtype as C */
@@ -158,6 +161,11 @@ typedef struct dk_matmul_epilogue {
   const int32_t* row_seq;  /* device int32[M]; NULL: row m writes cache sequence m */
   const int32_t* row_pos;  /* device int32[M]: token position written by row m */
   unsigned long long* argmax_keys;  /* DK_EPI_ARGMAX: device uint64[M] */
+  const void* norm_w;      /* DK_EPI_RESIDUAL_RMSNORM: weight [N] of norm_w_dtype */
+  int norm_w_dtype;
+  void* norm_out;          /* [M, N] rows norm_ld apart, dtype of C */
+  int64_t norm_ld;
+  float norm_eps;
 } dk_matmul_epilogue;
 
 /* dk_matmul_batch_invariant followed by the epilogue `epi` (same K numerics; NULL epi = DK_EPI_STORE).

@@ -134,3 +134,30 @@ def test_fused_rows_are_batch_invariant(dev):
     matmul_fused(a[:1].contiguous(), wg, "argmax", argmax_keys=keys)
     argmax_finish(keys, tok1)
     assert tok1.item() == tok[0].item()
+
+
+@pytest.mark.parametrize("dtype_name", ["bfloat16", "float16"])
+@pytest.mark.parametrize("mkn", SHAPES + [(256, 1024, 1024), (256, 2816, 1024), (5, 4096, 1000)])
+def test_residual_rmsnorm_equals_residual_then_rmsnorm(dev, dtype_name, mkn):
+    """The fused residual + RMSNorm epilogue gives the bits of the residual matmul followed by
+    rmsnorm_batch_invariant, with the residual in place or not and either weight dtype (the
+    split shapes take the one-kernel fold + norm; N = 1000 and the fold-schedule shapes take
+    the separate RMSNorm kernel)."""
+    import torch
+    from detkernels_b200.kernels.matmul import matmul_fused
+    from detkernels_b200.kernels.rmsnorm import rmsnorm_batch_invariant
+    dtype = getattr(torch, dtype_name)
+    m, k, n = mkn
+    a, b = _inputs(dev, m, k, n, dtype, seed=m + n)
+    r = torch.randn(m, n, device=dev, dtype=dtype)
+    for w_dtype in (dtype, torch.float32):
+        w = (1.0 + 0.1 * torch.randn(n, device=dev)).to(w_dtype)
+        h_ref = matmul_fused(a, b, "residual", residual=r)
+        y_ref = rmsnorm_batch_invariant(h_ref, w, 1e-6)
+        y = torch.empty_like(r)
+        h = matmul_fused(a, b, "residual_rmsnorm", residual=r, norm_weight=w, norm_out=y, eps=1e-6)
+        assert torch.equal(h, h_ref) and torch.equal(y, y_ref), (mkn, w_dtype)
+        inplace = r.clone()
+        y2 = torch.full_like(r, float("nan"))
+        matmul_fused(a, b, "residual_rmsnorm", residual=inplace, out=inplace, norm_weight=w, norm_out=y2, eps=1e-6)
+        assert torch.equal(inplace, h_ref) and torch.equal(y2, y_ref), (mkn, w_dtype)
