@@ -273,8 +273,10 @@ __device__ __forceinline__ int describe_item(const Params& p, int64_t w, Item& i
 // operands and order (per token the same 16-deep MMA dot products over the same
 // k steps; l from the same four tokens per lane, (p0 + p1) + (p2 + p3), and the
 // same butterfly), so a row's bits are those of the 16-row form.
+// Occupancy: 3 CTAs per SM for d <= 64, except the wide multi-row (prefill) instances
+// (KM >= 8), which run 2 per SM without register spills (measured faster).
 template <typename T, int D, int KM, bool T1>
-__global__ void __launch_bounds__(kThreads, (D == 128) ? 2 : 3)
+__global__ void __launch_bounds__(kThreads, (D == 128 || (!T1 && KM >= 8)) ? 2 : 3)
     attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const Params p) {
   using C = Cfg<D>;
   static_assert(KM <= C::KMAX, "merge elements per thread");
