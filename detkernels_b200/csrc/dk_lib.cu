@@ -438,7 +438,7 @@ AttnPlan plan_attention(int32_t n_tiles, int32_t rows_per_tile, int32_t hq, int3
 template <typename T, int D, int KM, bool T1>
 int attn_launch_km(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int64_t n_items,
                    cudaStream_t st) {
-  using C = dk::attn::Cfg<D>;
+  using C = dk::attn::Cfg<D, T1>;
   static bool done[kMaxDevices] = {false};
   static int resident[kMaxDevices][dk::attn::kRows + 1] = {};   // CTAs per SM, by rows_cap
   auto fn = dk::attn::attn_kernel<T, D, KM, T1>;
