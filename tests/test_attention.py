@@ -142,18 +142,22 @@ def test_baseline_config_tracked_sequence_bitwise(dev):
         del kc, vc
 
 
-def test_prefill_row_tiles_reproduce_decode_rows(dev):
+@pytest.mark.parametrize("dtype_name", ["bfloat16", "float16"])
+def test_prefill_row_tiles_reproduce_decode_rows(dev, dtype_name):
     """Rows of one sequence processed as a multi-row tile (prefill) give exactly
-    the bits of the same rows processed one per tile (decode)."""
+    the bits of the same rows processed one per tile (decode).  Without grouped
+    query heads the decode launch takes the single-row (transposed) kernel, so this
+    also pins that kernel to the 16-row form at d 32, 64 and 128."""
     import torch
     from detkernels_b200.kernels.attention import attention_decode
-    for (H, Hkv, D) in ((16, 16, 64), (32, 8, 128), (8, 8, 32)):
+    dtype = getattr(torch, dtype_name)
+    for (H, Hkv, D) in ((16, 16, 64), (32, 8, 128), (8, 8, 32), (8, 8, 128)):
         G = H // Hkv
         rows_per_tile = 16 // G
         S = 700
         g = torch.Generator(device=dev).manual_seed(H + D)
-        kc = torch.randn(2, Hkv, S, D, device=dev, generator=g).to(torch.bfloat16)
-        vc = torch.randn(2, Hkv, S, D, device=dev, generator=g).to(torch.bfloat16)
+        kc = torch.randn(2, Hkv, S, D, device=dev, generator=g).to(dtype)
+        vc = torch.randn(2, Hkv, S, D, device=dev, generator=g).to(dtype)
         # sequence 0: prompt positions 0..299 ; sequence 1: positions 0..S-1 at stride 7
         pos = [list(range(300)), list(range(0, S, 7))]
         rows_seq, rows_len, tiles = [], [], []
@@ -164,7 +168,7 @@ def test_prefill_row_tiles_reproduce_decode_rows(dev):
                 rows_seq += [sq] * len(chunk)
                 rows_len += [p + 1 for p in chunk]
         R = len(rows_seq)
-        q = torch.randn(R, H, D, device=dev, generator=g).to(torch.bfloat16)
+        q = torch.randn(R, H, D, device=dev, generator=g).to(dtype)
         lens = torch.tensor(rows_len, dtype=torch.int32, device=dev)
         tiles_t = torch.tensor(tiles, dtype=torch.int32, device=dev)
         out_tiled = attention_decode(q, kc, vc, lens, row_tiles=tiles_t, max_kv_len=S)
@@ -175,7 +179,8 @@ def test_prefill_row_tiles_reproduce_decode_rows(dev):
         assert torch.equal(out_tiled, out_rows), (H, Hkv, D)
         want = oracle.attention(q.float().cpu().numpy(), kc.float().cpu().numpy(), vc.float().cpu().numpy(),
                                 kv_lens=rows_len, row_seq=rows_seq)
-        np.testing.assert_allclose(out_tiled.float().cpu().numpy(), want, rtol=2 ** -6, atol=2 ** -6)
+        tol = 2 ** -6 if dtype == torch.bfloat16 else 2 ** -8
+        np.testing.assert_allclose(out_tiled.float().cpu().numpy(), want, rtol=tol, atol=tol)
 
 
 def test_batch_variant_row_can_diverge_across_batch_sizes(dev):
