@@ -81,6 +81,9 @@ SIGNATURES = {
 }
 
 
+# layout version of the structs mirrored here (DK_ABI_VERSION of include/detkernels_b200.h)
+ABI_VERSION = 2
+
 DK_EPI_STORE = 0
 DK_EPI_RESIDUAL = 1
 DK_EPI_SILU = 2
@@ -136,6 +139,11 @@ def load():
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
+        if lib.dk_abi_version() != ABI_VERSION:
+            raise DetKernelsError(
+                DK_ERR_UNSUPPORTED,
+                "detkernels_b200: %s has ABI version %d, this package needs %d; rebuild it with "
+                "`python -m detkernels_b200.build`" % (path, lib.dk_abi_version(), ABI_VERSION))
         _lib = lib
         return lib
 

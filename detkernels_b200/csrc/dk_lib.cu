@@ -552,7 +552,7 @@ int noalloc_scratch(void** out, const char* what) {
 // =====================================================================================
 extern "C" {
 
-int dk_abi_version(void) { return 1; }
+int dk_abi_version(void) { return DK_ABI_VERSION; }
 
 const char* dk_last_error(void) { return g_last_error.c_str(); }
 

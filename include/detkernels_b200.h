@@ -57,6 +57,9 @@ extern "C" {
 #define DK_RMSNORM_THREADS 256      /* one CTA of 256 threads per row */
 
 /* ---- library / device queries ---- */
+/* Layout version of this header's structs and signatures; dk_abi_version() of a library built from it
+ * returns the same number.  2: dk_matmul_epilogue gained the DK_EPI_RESIDUAL_RMSNORM fields. */
+#define DK_ABI_VERSION 2
 int dk_abi_version(void);
 /* Message for the last non-zero return code on the calling host thread. */
 const char* dk_last_error(void);
