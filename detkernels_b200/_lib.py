@@ -45,6 +45,8 @@ SIGNATURES = {
                                     ctypes.POINTER(_int)]),
     "dk_rmsnorm_batch_invariant": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _int,
                                           _f32, _c_void_p]),
+    "dk_rmsnorm_gather_batch_invariant": (_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64,
+                                                 _c_void_p, _i64, _i64, _i64, _int, _int, _f32, _c_void_p]),
     "dk_rmsnorm_variant_workspace_size": (_size, [_i64]),
     "dk_rmsnorm_batch_variant": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _int, _f32,
                                         _int, _int, _c_void_p, _size, _c_void_p]),

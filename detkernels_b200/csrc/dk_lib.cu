@@ -160,6 +160,25 @@ int rmsnorm_inv_launch(const void* x, int64_t xs, const void* w, void* y, int64_
 }
 
 template <typename T, typename W>
+int rmsnorm_gather_launch(const void* table, int64_t ts, int64_t table_rows, const int64_t* idx, const void* w,
+                          void* x, int64_t xs, void* y, int64_t ys, int64_t rows, int64_t cols, float eps,
+                          cudaStream_t st) {
+  constexpr int VEC = dk::Vec16<T>::N;
+  constexpr int MAXC = (sizeof(T) == 4) ? 8 : 4;
+  const bool vec = (cols % VEC == 0) && (ts % VEC == 0) && (xs % VEC == 0) && (ys % VEC == 0) && aligned16(table) &&
+                   aligned16(x) && aligned16(y) && cols <= static_cast<int64_t>(MAXC) * dk::kRmsThreads * VEC;
+  if (!vec)
+    return fail(DK_ERR_UNSUPPORTED,
+                "rmsnorm_gather: needs 16-byte aligned rows, n_cols a multiple of %d and at most %d", VEC,
+                MAXC * dk::kRmsThreads * VEC);
+  cudaError_t e = launch_pdl(dk::rmsnorm_gather_vec_kernel<T, W, MAXC>, dim3(static_cast<unsigned>(rows)),
+                             dim3(dk::kRmsThreads), 0, st, static_cast<const T*>(table), ts, table_rows, idx,
+                             static_cast<const W*>(w), static_cast<T*>(x), xs, static_cast<T*>(y), ys, cols, eps);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "rmsnorm_gather: launch failed: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
+
+template <typename T, typename W>
 int rmsnorm_var_launch(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int64_t cols,
                        float eps, int n_splits, float* partial, cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(partial, 0, sizeof(float) * rows, st);
@@ -612,6 +631,22 @@ int dk_rmsnorm_batch_invariant(const void* x, int64_t x_row_stride, const void* 
   if (n_rows == 0) return DK_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   DK_DISPATCH_RMS(rmsnorm_inv_launch, x, x_row_stride, weight, out, out_row_stride, n_rows, n_cols, eps, st);
+}
+
+int dk_rmsnorm_gather_batch_invariant(const void* table, int64_t table_row_stride, int64_t table_rows,
+                                      const int64_t* row_index, const void* weight, void* x_out, int64_t x_row_stride,
+                                      void* out, int64_t out_row_stride, int64_t n_rows, int64_t n_cols, int dtype,
+                                      int wdtype, float eps, void* stream) {
+  int rc = rms_validate(table, weight, out, table_row_stride, out_row_stride, n_rows, n_cols, dtype, wdtype,
+                        "rmsnorm_gather");
+  if (rc) return rc;
+  if (n_rows == 0) return DK_OK;
+  if (!row_index || !x_out || table_rows <= 0 || (n_rows > 1 && x_row_stride < n_cols) ||
+      (table_rows > 1 && table_row_stride < n_cols))
+    return fail(DK_ERR_INVALID_ARGUMENT, "rmsnorm_gather: bad index, table or x_out");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  DK_DISPATCH_RMS(rmsnorm_gather_launch, table, table_row_stride, table_rows, row_index, weight, x_out, x_row_stride,
+                  out, out_row_stride, n_rows, n_cols, eps, st);
 }
 
 size_t dk_rmsnorm_variant_workspace_size(int64_t n_rows) {

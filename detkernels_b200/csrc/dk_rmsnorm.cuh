@@ -112,6 +112,64 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_inv_vec_kernel(const T* _
   }
 }
 
+// Embedding lookup fused into the invariant RMSNorm: row r reads table row idx[r], copies it
+// to x_out (the residual stream) and normalises it with exactly rmsnorm_inv_vec_kernel's
+// arithmetic.  An index outside [0, table_rows) records DK_ERR_DEVICE_CHECK and leaves the
+// row untouched.  Vector path only: 16-byte aligned rows, n_cols <= MAXC * 256 * VEC.
+template <typename T, typename W, int MAXC>
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_gather_vec_kernel(const T* __restrict__ table, int64_t ts,
+                                                                          int64_t table_rows,
+                                                                          const int64_t* __restrict__ idx,
+                                                                          const W* __restrict__ w, T* __restrict__ x,
+                                                                          int64_t xs, T* __restrict__ y, int64_t ys,
+                                                                          int64_t n_cols, float eps) {
+  pdl_wait();   // the indices may come from the previous kernel
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  constexpr int VEC = Vec16<T>::N;
+  __shared__ float red[9];
+  const int64_t row = blockIdx.x;
+  const int64_t src = idx[row];
+  if (src < 0 || src >= table_rows) {
+    if (threadIdx.x == 0) report_error(DK_ERR_DEVICE_CHECK, 0x300);
+    return;
+  }
+  const T* tr = table + src * ts;
+  T* xr = x + row * xs;
+  T* yr = y + row * ys;
+  const int64_t nchunks = n_cols / VEC;
+  Vec16<T> keep[MAXC];
+  float acc = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int64_t c = threadIdx.x + (int64_t)i * kRmsThreads;
+    if (c < nchunks) {
+      keep[i] = *reinterpret_cast<const Vec16<T>*>(tr + c * VEC);
+      *reinterpret_cast<Vec16<T>*>(xr + c * VEC) = keep[i];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float f = to_f32<T>(keep[i].v[j]);
+        acc = __fmaf_rn(f, f, acc);
+      }
+    }
+  }
+  const float total = block_sum_256(acc, red);
+  const float var = __fdiv_rn(total, (float)n_cols);
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int64_t c = threadIdx.x + (int64_t)i * kRmsThreads;
+    if (c < nchunks) {
+      Vec16<T> o;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float xn = __fmul_rn(to_f32<T>(keep[i].v[j]), rstd);
+        o.v[j] = from_f32<T>(__fmul_rn(xn, to_f32<W>(w[c * VEC + j])));
+      }
+      *reinterpret_cast<Vec16<T>*>(yr + c * VEC) = o;
+    }
+  }
+}
+
 // Scalar path for unaligned rows or n_cols not a multiple of the vector width.
 // It walks the same 16-byte chunks in the same per-thread order as the vector
 // path (the last chunk may be short), so a row's bits do not depend on which

@@ -64,6 +64,34 @@ def rmsnorm_batch_invariant(x, weight, eps: float = 1e-6):
     return out.reshape(orig_shape)
 
 
+def rmsnorm_gather(table, index, weight, eps: float = 1e-6, x_out=None, out=None):
+    """Embedding lookup fused into the batch-invariant RMSNorm: returns (x, y) with
+    x = table[index] and y = rmsnorm_batch_invariant(x, weight, eps), bit for bit, from one
+    launch.  index: int64 CUDA tensor [n]; an index outside the table sets the device status."""
+    import torch
+
+    assert table.is_cuda and index.is_cuda and weight.is_cuda, "rmsnorm_gather requires CUDA tensors"
+    assert table.dim() == 2 and table.stride(1) == 1 and index.dtype == torch.int64 and index.dim() == 1
+    n, h = index.numel(), table.shape[1]
+    assert weight.numel() == h
+    w = weight.reshape(-1).contiguous()
+    idx = index.contiguous()
+    if x_out is None:
+        x_out = torch.empty((n, h), dtype=table.dtype, device=table.device)
+    if out is None:
+        out = torch.empty((n, h), dtype=table.dtype, device=table.device)
+    assert x_out.shape == (n, h) and out.shape == (n, h) and x_out.stride(1) == 1 and out.stride(1) == 1
+    if n == 0:
+        return x_out, out
+    rc = _lib.load().dk_rmsnorm_gather_batch_invariant(
+        table.data_ptr(), table.stride(0), table.shape[0], idx.data_ptr(), w.data_ptr(), x_out.data_ptr(),
+        x_out.stride(0), out.data_ptr(), out.stride(0), n, h, _lib.dtype_code(table.dtype), _lib.dtype_code(w.dtype),
+        float(eps), _lib.stream_ptr(table.device))
+    _lib.check(rc, "rmsnorm_gather")
+    _lib.count_launch()
+    return x_out, out
+
+
 def rmsnorm_batch_variant(x, weight, eps: float = 1e-6, split_threshold: int = 16, n_splits: int = 4):
     """Deliberately batch-variant RMSNorm: split + f32 atomics when n_rows < split_threshold."""
     orig_shape, x2d, w, out = _prepare(x, weight, "rmsnorm_batch_variant")

@@ -32,7 +32,7 @@ from typing import List, Optional, Sequence
 
 from .attention import attention_batch_invariant, attention_batch_variant, attention_decode, attention_reference
 from .matmul import argmax_finish, matmul_batch_invariant, matmul_batch_variant, matmul_fused, matmul_reference
-from .rmsnorm import rmsnorm_batch_invariant, rmsnorm_batch_variant, rmsnorm_reference
+from .rmsnorm import rmsnorm_batch_invariant, rmsnorm_batch_variant, rmsnorm_gather, rmsnorm_reference
 
 _KERNEL_SETS = {
     "batch_invariant": {
@@ -386,8 +386,7 @@ class DecodeEngine:
         saved = self.gemm_ws
         self.gemm_ws = plan["gemm_ws"]
         try:
-            x = self.model.embed[plan["tok"]]
-            xn = rmsnorm_batch_invariant(x, self.layers[0]["norm1_w"], self.cfg.eps)
+            x, xn = rmsnorm_gather(self.model.embed, plan["tok"], self.layers[0]["norm1_w"], self.cfg.eps)
             for li, layer in enumerate(self.layers):
                 x, xn = self._layer(li, layer, x, xn, plan["rows32"], plan["pos32"], plan["q_lens"], plan["tiles"],
                                     plan["max_len"], plan["attn_ws"])
@@ -406,8 +405,7 @@ class DecodeEngine:
         step (sizes the attention grid)."""
         import torch
 
-        x = self.model.embed[self.tokens]
-        xn = rmsnorm_batch_invariant(x, self.layers[0]["norm1_w"], self.cfg.eps)
+        x, xn = rmsnorm_gather(self.model.embed, self.tokens, self.layers[0]["norm1_w"], self.cfg.eps)
         for li, layer in enumerate(self.layers):
             ev = None
             if events is not None:

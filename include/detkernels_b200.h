@@ -82,6 +82,17 @@ int dk_rmsnorm_batch_invariant(const void* x, int64_t x_row_stride, const void* 
                                int64_t out_row_stride, int64_t n_rows, int64_t n_cols, int dtype,
                                int weight_dtype, float eps, void* stream);
 
+/* Embedding lookup + invariant RMSNorm: x_out[r, :] = table[row_index[r], :] and out[r, :] =
+ * dk_rmsnorm_batch_invariant(x_out[r, :]), the same bits as the lookup followed by that call, in one
+ * launch.  row_index: device int64[n_rows]; an index outside [0, table_rows) sets the device status
+ * (DK_ERR_DEVICE_CHECK) and leaves its row unwritten.  Needs 16-byte aligned rows and n_cols a multiple
+ * of 16 bytes (DK_ERR_UNSUPPORTED otherwise).  No counterpart in the reference: it fuses the decoder's
+ * `self.embed[token_ids]` (kernels/tiny_model.py:110) into the first block's input norm. */
+int dk_rmsnorm_gather_batch_invariant(const void* table, int64_t table_row_stride, int64_t table_rows,
+                                      const int64_t* row_index, const void* weight, void* x_out, int64_t x_row_stride,
+                                      void* out, int64_t out_row_stride, int64_t n_rows, int64_t n_cols, int dtype,
+                                      int wdtype, float eps, void* stream);
+
 /* Scratch bytes dk_rmsnorm_batch_variant needs for n_rows rows. */
 size_t dk_rmsnorm_variant_workspace_size(int64_t n_rows);
 /* replaces kernels/rmsnorm.py:180-218 rmsnorm_batch_variant: when n_rows < split_threshold each row's

@@ -132,3 +132,30 @@ def test_requires_cuda_tensor():
     from detkernels_b200.kernels.rmsnorm import rmsnorm_batch_invariant
     with pytest.raises(AssertionError):
         rmsnorm_batch_invariant(torch.randn(2, 8), torch.randn(8))
+
+
+@pytest.mark.parametrize("dtype_name,w_name", [("bfloat16", "bfloat16"), ("float16", "float32"), ("float32", "float32")])
+def test_gather_equals_lookup_then_rmsnorm(dev, dtype_name, w_name):
+    """The fused embedding lookup + RMSNorm gives the bits of table[index] followed by
+    rmsnorm_batch_invariant, for repeated and arbitrary indices; an index outside the
+    table is caught by the kernel's check (status DK_ERR_DEVICE_CHECK, nothing written)."""
+    import torch
+    from detkernels_b200 import _lib
+    from detkernels_b200.kernels.rmsnorm import rmsnorm_batch_invariant, rmsnorm_gather
+    dtype, w_dtype = getattr(torch, dtype_name), getattr(torch, w_name)
+    g = torch.Generator(device=dev).manual_seed(11)
+    table = torch.randn(1000, 1024, device=dev, generator=g).to(dtype)
+    w = (1.0 + 0.1 * torch.randn(1024, device=dev, generator=g)).to(w_dtype)
+    for n in (1, 7, 256):
+        idx = torch.randint(0, 1000, (n,), device=dev, generator=g)
+        idx[0] = idx[-1]
+        x, y = rmsnorm_gather(table, idx, w, 1e-6)
+        assert torch.equal(x, table[idx])
+        assert torch.equal(y, rmsnorm_batch_invariant(table[idx], w, 1e-6))
+    bad = torch.tensor([3, 1000], device=dev, dtype=torch.int64)
+    x = torch.zeros(2, 1024, device=dev, dtype=dtype)
+    y = torch.zeros(2, 1024, device=dev, dtype=dtype)
+    rmsnorm_gather(table, bad, w, 1e-6, x_out=x, out=y)
+    code, _ = _lib.device_status(torch.cuda.current_device(), clear=True)
+    assert code == _lib.DK_ERR_DEVICE_CHECK
+    assert torch.equal(x[0], table[3]) and int(x[1].count_nonzero()) == 0 and int(y[1].count_nonzero()) == 0
