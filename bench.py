@@ -11,8 +11,8 @@ collective in the data path); the device-timed max over ranks is reported.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-``--impl reference`` times the CPU path of the reference's algorithm (the
-numpy oracle) on the host cores for the same metric.
+``--impl reference`` times the reference's decode step (its eager torch
+formulas) on the host cores over the same 256 sequences, for the same metric.
 """
 from __future__ import annotations
 
@@ -37,7 +37,16 @@ OTHER_LEN = (16, 512)
 NEW_TOKENS = 128
 WORKLOAD_NAME = ("tinymodel-decode: 4L d1024 16x64 SwiGLU2816 vocab32000 bf16, 256 prompts/GPU "
                  "(tracked 32 tok + 255 of U[16,512] tok), 128 greedy tokens")
+# inputs vs L2: the KV cache (4 layers x 256 seq x 16 heads x 640 tokens x 64 x bf16 x K,V = 2.7 GB)
+# and the weights (168 MB) both exceed the 126 MB L2, so no flush is needed between steps
+L2_NOTE = "inputs larger than L2 (KV cache 2.7 GB/GPU, weights 168 MB)"
 GEMM_SHAPES = [(m, n) for n in (4096, 11008) for m in (1, 8, 64, 256, 2048)]
+
+
+def workload_config(world: int = 1):
+    """The `config` object of both arms' JSON lines (same keys and values at one GPU)."""
+    return {"workload": WORKLOAD_NAME, "global_batch": BATCH_PER_GPU * world, "new_tokens": NEW_TOKENS,
+            "l2": L2_NOTE}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -194,9 +203,107 @@ def cpu_sample(prompts, n_tokens, model=None):
 
 
 def cpu_sample_prompts():
-    """Bounded CPU sample: the tracked prompt and 7 co-batched prompts cut to 48 tokens."""
+    """Small parity sample for the oracle check: the tracked prompt and 7 co-batched prompts cut to 48 tokens."""
     p = make_prompts(0, 8)
     return [p[0]] + [q[:48] for q in p[1:]]
+
+
+class ReferenceDecodeCPU:
+    """The reference's decode step on the host cores, at the workload's batch and KV lengths.
+
+    Each step is the reference's ``TinyModel.forward_step`` (kernels/tiny_model.py:99-140) built
+    from its eager formulas (``rmsnorm_reference``, ``matmul_reference``, ``attention_reference``;
+    kernels/rmsnorm.py:39-48, kernels/matmul.py:42-49, kernels/attention.py:49-71) with the
+    workload's SwiGLU MLP, over all 256 sequences at once.  The reference grows one KV tensor per
+    layer with ``torch.cat`` and has no ragged batches, so here each sequence keeps its own
+    unpadded [H, len, D] cache (preallocated for the steps that run) and attention is the
+    reference formula on that sequence's cache.  The caches start at the prompt lengths of the
+    workload, filled with seeded N(0,1) values: the reference has no prefill, so the prompts'
+    prefill is not part of this arm (the GPU arm's steps include it).
+    """
+
+    def __init__(self, model, prompts, max_steps, threads):
+        import numpy as np
+        import torch
+
+        self.model, self.threads = model, threads
+        cfg = model.config
+        self.B = len(prompts)
+        self.H, self.Hkv, self.D = cfg.num_heads, cfg.kv_heads, cfg.head_dim
+        self.lens0 = np.array([len(p) for p in prompts], dtype=np.int64)
+        g = torch.Generator().manual_seed(1234)
+        self.k = [[torch.randn(self.Hkv, int(L) + max_steps, self.D, generator=g).to(model.dtype)
+                   for L in self.lens0] for _ in range(cfg.num_layers)]
+        self.v = [[torch.randn(self.Hkv, int(L) + max_steps, self.D, generator=g).to(model.dtype)
+                   for L in self.lens0] for _ in range(cfg.num_layers)]
+        self.max_steps = max_steps
+        self.first = torch.tensor([p[-1] for p in prompts], dtype=torch.long)
+
+    def _step(self, tok, lens):
+        import torch
+
+        from detkernels_b200.kernels.attention import attention_reference
+        from detkernels_b200.kernels.matmul import matmul_reference as mm
+        from detkernels_b200.kernels.rmsnorm import rmsnorm_reference as rms
+
+        m, cfg = self.model, self.model.config
+        B, H, Hkv, D = self.B, self.H, self.Hkv, self.D
+        x = m.embed[tok]
+        for li, L in enumerate(m.layers):
+            xn = rms(x, L["norm1_w"], cfg.eps)
+            q = mm(xn, L["w_q"]).view(B, H, D)
+            kn = mm(xn, L["w_k"]).view(B, Hkv, D)
+            vn = mm(xn, L["w_v"]).view(B, Hkv, D)
+            outs = []
+            for b in range(B):
+                n = int(lens[b])
+                kb, vb = self.k[li][b], self.v[li][b]
+                kb[:, n] = kn[b]
+                vb[:, n] = vn[b]
+                outs.append(attention_reference(q[b:b + 1], kb[None, :, :n + 1], vb[None, :, :n + 1]))
+            a = torch.cat(outs).reshape(B, H * D)
+            x = x + mm(a, L["w_o"])
+            xn = rms(x, L["norm2_w"], cfg.eps)
+            if cfg.mlp == "swiglu":
+                hid = torch.nn.functional.silu(mm(xn, L["w_gate"])) * mm(xn, L["w_up"])
+            else:
+                hid = torch.nn.functional.silu(mm(xn, L["w_mlp1"]))
+            x = x + mm(hid, L["w_mlp2"])
+        logits = mm(rms(x, m.norm_f_w, cfg.eps), m.w_lm_head)
+        return logits.argmax(dim=-1)
+
+    def run(self, n_steps):
+        """n_steps greedy decode steps over all sequences from the prompt lengths; returns seconds."""
+        import torch
+
+        assert n_steps <= self.max_steps
+        torch.set_num_threads(self.threads)
+        lens = self.lens0.copy()
+        tok = self.first.clone()
+        t0 = time.perf_counter()
+        with torch.inference_mode():
+            for _ in range(n_steps):
+                tok = self._step(tok, lens)
+                lens += 1
+        return time.perf_counter() - t0
+
+    def describe(self, n_steps):
+        return ("reference eager formulas (torch, %d host threads): %d greedy decode steps x %d sequences "
+                "from KV lengths %d..%d (prefill excluded)" % (self.threads, n_steps, self.B, int(self.lens0.min()),
+                                                               int(self.lens0.max())))
+
+
+def cpu_baseline_sample(model=None, n_steps=32):
+    """cpu_baseline of the GPU line: one bounded sample (~10-30 s) of ReferenceDecodeCPU."""
+    from detkernels_b200.kernels.tiny_model import TinyModel, TinyModelConfig
+
+    threads = len(os.sched_getaffinity(0))
+    cpu_model = TinyModel(TinyModelConfig(**MODEL), device="cpu")
+    ref = ReferenceDecodeCPU(cpu_model, make_prompts(0, BATCH_PER_GPU), n_steps, threads)
+    ref.run(1)   # warm-up
+    dt = ref.run(n_steps)
+    return {"value": ref.B * n_steps / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": ref.describe(n_steps) + ", %.1f s" % dt}
 
 
 # ----------------------------------------------------------------------------- GEMM vs cuBLAS
@@ -333,25 +440,33 @@ def gdn_bench(peaks, iters=3):
 
 
 # ----------------------------------------------------------------------------- main arms
+REF_DECODE_STEPS = 4   # decode steps per timed step of the reference arm (B = 256 each)
+
+
 def run_reference(args, rank, world):
-    """CPU path of the reference algorithm (numpy oracle), rank 0 only."""
+    """The reference's decode step on the host cores (ReferenceDecodeCPU), rank 0 only: each
+    step is REF_DECODE_STEPS greedy decode steps of the 256 workload sequences."""
     if rank != 0:
         return 0
-    prompts = cpu_sample_prompts()
-    vals = []
-    base = None
+    from detkernels_b200.kernels.tiny_model import TinyModel, TinyModelConfig
+
+    threads = len(os.sched_getaffinity(0))
+    model = TinyModel(TinyModelConfig(**MODEL), device="cpu")
+    ref = ReferenceDecodeCPU(model, make_prompts(0, BATCH_PER_GPU), REF_DECODE_STEPS, threads)
+    secs = []
     for i in range(args.warmup + args.steps):
-        cb, _ = cpu_sample(prompts, 16)
+        dt = ref.run(REF_DECODE_STEPS)
         if i >= args.warmup:
-            vals.append(cb["value"])
-            base = cb
-    value = statistics.mean(vals)
-    base["value"] = value
+            secs.append(dt)
+    total = sum(secs)
+    value = ref.B * REF_DECODE_STEPS * len(secs) / total
+    sample = ref.describe(REF_DECODE_STEPS) + " per step"
     line = {"impl": "reference", "metric": "BI decode tok/s", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD_NAME, "sample": base["sample"]},
-            "cpu_baseline": base,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / len(secs) * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random prompts, random-init weights)",
+            "config": workload_config(1), "parallelism": "host cores (%d threads)" % threads, "sample": sample,
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -472,8 +587,9 @@ def run_ours(args, rank, world, local):
                 "algorithmic_bytes_per_launch": int(avg_bytes),
                 "share_of_step": round(attn_ms / ms_per_step, 3)}
 
-    cpu, cpu_toks = (cpu_sample(cpu_sample_prompts(), 16, model) if world == 1 and not args.skip_cpu
-                     else (None, None))
+    cpu = cpu_baseline_sample() if world == 1 and not args.skip_cpu else None
+    _, cpu_toks = (cpu_sample(cpu_sample_prompts(), 16, model) if world == 1 and not args.skip_cpu
+                   else (None, None))
     parity = None
     if cpu_toks is not None:
         ours_small = model.generate(cpu_sample_prompts(), 16, "batch_invariant").cpu().numpy()
@@ -488,10 +604,7 @@ def run_ours(args, rank, world, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random prompts, random-init weights)",
-        "config": {"workload": WORKLOAD_NAME, "global_batch": BATCH_PER_GPU * world,
-                   "new_tokens": NEW_TOKENS, "parallelism": "dp%d (request-sharded, no collective)" % world,
-                   "l2": "inputs larger than L2 (KV cache %.1f GB/GPU, weights 168 MB)"
-                         % (eng.k_cache[0].numel() * 2 * 2 * MODEL["num_layers"] / 1e9)},
+        "config": workload_config(world), "parallelism": "dp%d (request-sharded, no collective)" % world,
         "e2e": {"value": e2e_value and round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),

@@ -41,6 +41,7 @@ SIGNATURES = {
     "dk_last_error": (ctypes.c_char_p, []),
     "dk_device_status": (_int, [_int, _int, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
     "dk_num_sms": (_int, [_int, ctypes.POINTER(_int)]),
+    "dk_test_bounded_wait": (_int, [_int, _i64, _c_void_p]),
     "dk_kernel_attributes": (_int, [_int, ctypes.POINTER(_int), ctypes.POINTER(_int), ctypes.POINTER(_int),
                                     ctypes.POINTER(_int)]),
     "dk_rmsnorm_batch_invariant": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _int,
@@ -123,7 +124,9 @@ def library_path() -> str:
 
 
 def load():
-    """Load (building first if this checkout has nvcc and a stale library)."""
+    """Load the in-tree library (it is never built here: ``python -m detkernels_b200.build``
+    or ``__graft_entry__.build()`` builds it).  A missing library, a library of another ABI
+    version or one that lacks a declared entry point raises DetKernelsError."""
     global _lib
     if _lib is not None:
         return _lib
@@ -131,21 +134,33 @@ def load():
         if _lib is not None:
             return _lib
         path = library_path()
+        rebuild = "rebuild it with `python -m detkernels_b200.build`"
         if not os.path.exists(path):
             raise DetKernelsError(
                 DK_ERR_CUDA,
                 "detkernels_b200: %s is not built; run `python -m detkernels_b200.build` "
                 "(there is no CPU or eager fallback)" % path)
         lib = ctypes.CDLL(path)
-        for name, (res, args) in SIGNATURES.items():
-            fn = getattr(lib, name)
-            fn.restype = res
-            fn.argtypes = args
-        if lib.dk_abi_version() != ABI_VERSION:
+        try:
+            version_fn = lib.dk_abi_version
+        except AttributeError:
+            raise DetKernelsError(DK_ERR_UNSUPPORTED, "detkernels_b200: %s exports no dk_abi_version; %s"
+                                  % (path, rebuild)) from None
+        version_fn.restype = _int
+        version_fn.argtypes = []
+        if version_fn() != ABI_VERSION:
             raise DetKernelsError(
                 DK_ERR_UNSUPPORTED,
-                "detkernels_b200: %s has ABI version %d, this package needs %d; rebuild it with "
-                "`python -m detkernels_b200.build`" % (path, lib.dk_abi_version(), ABI_VERSION))
+                "detkernels_b200: %s has ABI version %d, this package needs %d; %s"
+                % (path, version_fn(), ABI_VERSION, rebuild))
+        for name, (res, args) in SIGNATURES.items():
+            try:
+                fn = getattr(lib, name)
+            except AttributeError:
+                raise DetKernelsError(DK_ERR_UNSUPPORTED, "detkernels_b200: %s lacks %s (a stale build); %s"
+                                      % (path, name, rebuild)) from None
+            fn.restype = res
+            fn.argtypes = args
         _lib = lib
         return lib
 

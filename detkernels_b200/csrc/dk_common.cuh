@@ -121,10 +121,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity.  Returns false (and records
-// a timeout) if the phase does not complete within kWaitLimitNs, or if another
+// a timeout) if the phase does not complete within limit_ns, or if another
 // thread already recorded an error.  `abort_flag` lets a thread skip all later
 // waits once one has failed, so a broken pipeline unwinds in one limit period.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int detail, bool& abort_flag) {
+// The library's kernels wait through mbar_wait (limit kWaitLimitNs); the device
+// self-test (dk_test_bounded_wait) runs the same loop with a short limit.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int detail, bool& abort_flag,
+                                                unsigned long long limit_ns) {
   if (abort_flag) return false;
   const uint32_t b = smem_u32(bar);
   if (mbar_test_wait(b, parity)) return true;   // the common case: already complete
@@ -142,11 +145,36 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int de
       abort_flag = true;
       return false;
     }
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       report_error(DK_ERR_DEVICE_TIMEOUT, detail);
       abort_flag = true;
       return false;
     }
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int detail, bool& abort_flag) {
+  return mbar_wait_limit(bar, parity, detail, abort_flag, kWaitLimitNs);
+}
+
+// Self-test of the bounded wait: warp 0 waits on an mbarrier that expects one arrival;
+// warp 1's lane 0 arrives unless skip_arrive is set.  With skip_arrive the wait runs out
+// after limit_ns, records DK_ERR_DEVICE_TIMEOUT (detail kSelfTestDetail) and the kernel
+// returns normally; otherwise the wait completes and the status stays clean.
+constexpr int kSelfTestDetail = 0x7E57;
+
+__global__ void __launch_bounds__(64) bounded_wait_selftest_kernel(int skip_arrive, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    bool abort_flag = false;
+    mbar_wait_limit(&bar, 0, kSelfTestDetail, abort_flag, limit_ns);
+  } else if (threadIdx.x == 32 && !skip_arrive) {
+    mbar_arrive(&bar);
   }
 }
 

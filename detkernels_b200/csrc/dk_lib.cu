@@ -167,13 +167,15 @@ int rmsnorm_gather_launch(const void* table, int64_t ts, int64_t table_rows, con
   constexpr int MAXC = (sizeof(T) == 4) ? 8 : 4;
   const bool vec = (cols % VEC == 0) && (ts % VEC == 0) && (xs % VEC == 0) && (ys % VEC == 0) && aligned16(table) &&
                    aligned16(x) && aligned16(y) && cols <= static_cast<int64_t>(MAXC) * dk::kRmsThreads * VEC;
-  if (!vec)
-    return fail(DK_ERR_UNSUPPORTED,
-                "rmsnorm_gather: needs 16-byte aligned rows, n_cols a multiple of %d and at most %d", VEC,
-                MAXC * dk::kRmsThreads * VEC);
-  cudaError_t e = launch_pdl(dk::rmsnorm_gather_vec_kernel<T, W, MAXC>, dim3(static_cast<unsigned>(rows)),
-                             dim3(dk::kRmsThreads), 0, st, static_cast<const T*>(table), ts, table_rows, idx,
-                             static_cast<const W*>(w), static_cast<T*>(x), xs, static_cast<T*>(y), ys, cols, eps);
+  cudaError_t e;
+  if (vec)
+    e = launch_pdl(dk::rmsnorm_gather_vec_kernel<T, W, MAXC>, dim3(static_cast<unsigned>(rows)),
+                   dim3(dk::kRmsThreads), 0, st, static_cast<const T*>(table), ts, table_rows, idx,
+                   static_cast<const W*>(w), static_cast<T*>(x), xs, static_cast<T*>(y), ys, cols, eps);
+  else
+    e = launch_pdl(dk::rmsnorm_gather_scalar_kernel<T, W>, dim3(static_cast<unsigned>(rows)),
+                   dim3(dk::kRmsThreads), 0, st, static_cast<const T*>(table), ts, table_rows, idx,
+                   static_cast<const W*>(w), static_cast<T*>(x), xs, static_cast<T*>(y), ys, cols, eps);
   if (e != cudaSuccess) return fail(DK_ERR_CUDA, "rmsnorm_gather: launch failed: %s", cudaGetErrorString(e));
   return DK_OK;
 }
@@ -611,6 +613,14 @@ int dk_kernel_attributes(int which, int* num_regs, int* max_threads, int* local_
   if (local_bytes) *local_bytes = static_cast<int>(a.localSizeBytes);
   if (max_dynamic_smem) *max_dynamic_smem = a.maxDynamicSharedSizeBytes;
   return DK_OK;
+}
+
+int dk_test_bounded_wait(int skip_arrive, int64_t limit_ns, void* stream) {
+  if (limit_ns <= 0 || limit_ns > 100000000LL)
+    return fail(DK_ERR_INVALID_ARGUMENT, "dk_test_bounded_wait: limit_ns must be in (0, 100 ms]");
+  dk::bounded_wait_selftest_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(
+      skip_arrive ? 1 : 0, static_cast<unsigned long long>(limit_ns));
+  return check_launch("dk_test_bounded_wait");
 }
 
 int dk_num_sms(int device, int* out) {
@@ -1101,6 +1111,20 @@ int dk_attention_batch_variant(const void* q, int64_t q_stride_b, int64_t q_stri
 // device address is looked up once per device with cudaGetSymbolAddress and cached.
 // ---------------------------------------------------------------------------------------------
 size_t dk_attention_noalloc_scratch_limit(void) { return kNoAllocScratchBytes; }
+
+// Test hook, deliberately absent from the public header: writes `value` into the first `bytes`
+// bytes of the no-alloc scratch on the current device (synchronously), so a test can show that
+// the next no-alloc call clears the arrival counters it relies on.
+int dk_noalloc_scratch_fill_for_test(int value, size_t bytes) {
+  if (bytes > kNoAllocScratchBytes) return fail(DK_ERR_INVALID_ARGUMENT, "fill beyond the no-alloc scratch");
+  void* p = nullptr;
+  int rc = noalloc_scratch(&p, "dk_noalloc_scratch_fill_for_test");
+  if (rc) return rc;
+  cudaError_t e = cudaMemset(p, value & 0xff, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "dk_noalloc_scratch_fill_for_test: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
 
 int dk_attention_batch_invariant_noalloc(const void* q, int64_t q_stride_row, int64_t q_stride_head, const void* k,
                                          const void* v, int64_t kv_stride_seq, int64_t kv_stride_head,

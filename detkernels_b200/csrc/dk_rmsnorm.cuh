@@ -207,6 +207,55 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_inv_scalar_kernel(const T
   }
 }
 
+// Embedding lookup + invariant RMSNorm for rows the vector gather cannot take (unaligned
+// table or output rows, n_cols not a multiple of the vector width, or longer than the
+// vector kernel keeps in registers): the chunk walk of rmsnorm_inv_scalar_kernel, reading
+// table row idx[r] and copying it to x_out, so the bits equal the lookup followed by the
+// invariant RMSNorm on either path.
+template <typename T, typename W>
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_gather_scalar_kernel(const T* __restrict__ table, int64_t ts,
+                                                                             int64_t table_rows,
+                                                                             const int64_t* __restrict__ idx,
+                                                                             const W* __restrict__ w,
+                                                                             T* __restrict__ x, int64_t xs,
+                                                                             T* __restrict__ y, int64_t ys,
+                                                                             int64_t n_cols, float eps) {
+  pdl_wait();   // the indices may come from the previous kernel
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  constexpr int VEC = Vec16<T>::N;
+  __shared__ float red[9];
+  const int64_t row = blockIdx.x;
+  const int64_t src = idx[row];
+  if (src < 0 || src >= table_rows) {
+    if (threadIdx.x == 0) report_error(DK_ERR_DEVICE_CHECK, 0x301);
+    return;
+  }
+  const T* tr = table + src * ts;
+  T* xr = x + row * xs;
+  T* yr = y + row * ys;
+  const int64_t nchunks = (n_cols + VEC - 1) / VEC;
+  float acc = 0.0f;
+  for (int64_t c = threadIdx.x; c < nchunks; c += kRmsThreads) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const int64_t e = c * VEC + j;
+      if (e < n_cols) {
+        const T v = tr[e];
+        xr[e] = v;
+        const float f = to_f32<T>(v);
+        acc = __fmaf_rn(f, f, acc);
+      }
+    }
+  }
+  const float total = block_sum_256(acc, red);
+  const float var = __fdiv_rn(total, (float)n_cols);
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  for (int64_t e = threadIdx.x; e < n_cols; e += kRmsThreads) {
+    const float xn = __fmul_rn(to_f32<T>(tr[e]), rstd);
+    yr[e] = from_f32<T>(__fmul_rn(xn, to_f32<W>(w[e])));
+  }
+}
+
 // ---- batch-variant twin: split partial sums combined with atomics ----
 template <typename T>
 __global__ void __launch_bounds__(kRmsThreads) rmsnorm_var_partial_kernel(const T* __restrict__ x, int64_t xs,

@@ -34,25 +34,32 @@ def attention_reference(q, k, v, scale: float | None = None, *, kv_lens=None):
     if scale is None:
         scale = 1.0 / (d ** 0.5)
     q32 = q.to(torch.float32)
-    k32 = k.to(torch.float32)
-    v32 = v.to(torch.float32)
     H, Hkv = q.shape[1], k.shape[1]
-    if Hkv != H:
-        k32 = k32.repeat_interleave(H // Hkv, dim=1)
-        v32 = v32.repeat_interleave(H // Hkv, dim=1)
     if kv_lens is None:
+        k32 = k.to(torch.float32)
+        v32 = v.to(torch.float32)
+        if Hkv != H:
+            k32 = k32.repeat_interleave(H // Hkv, dim=1)
+            v32 = v32.repeat_interleave(H // Hkv, dim=1)
         scores = torch.einsum("bhd,bhsd->bhs", q32, k32) * scale
         probs = torch.softmax(scores, dim=-1)
         out = torch.einsum("bhs,bhsd->bhd", probs, v32)
         return out.to(orig_dtype)
+    # ragged rows: each row's own prefix of the cache, converted and expanded alone (the padding
+    # beyond a row's length is never touched)
     outs = []
     for b in range(q.shape[0]):
         L = int(kv_lens[b])
         if L == 0:
             outs.append(torch.zeros_like(q32[b]))
             continue
-        s = torch.einsum("hd,hsd->hs", q32[b], k32[b, :, :L]) * scale
-        outs.append(torch.einsum("hs,hsd->hd", torch.softmax(s, dim=-1), v32[b, :, :L]))
+        kb = k[b, :, :L].to(torch.float32)
+        vb = v[b, :, :L].to(torch.float32)
+        if Hkv != H:
+            kb = kb.repeat_interleave(H // Hkv, dim=0)
+            vb = vb.repeat_interleave(H // Hkv, dim=0)
+        s = torch.einsum("hd,hsd->hs", q32[b], kb) * scale
+        outs.append(torch.einsum("hs,hsd->hd", torch.softmax(s, dim=-1), vb))
     return torch.stack(outs).to(orig_dtype)
 
 

@@ -71,6 +71,12 @@ int dk_num_sms(int device, int* out);
  * launch-time thread limit, local-memory bytes, dynamic shared-memory limit).  which: 0 = bf16
  * GEMM, 1 = bf16 decode attention d128, 2 = bf16 decode attention d64, 3 = f32 RMSNorm. */
 int dk_kernel_attributes(int which, int* num_regs, int* max_threads, int* local_bytes, int* max_dynamic_smem);
+/* Self-test of the device-side bounded wait that every kernel of this library uses: one CTA waits on
+ * a shared-memory barrier for at most limit_ns (0 < limit_ns <= 100 ms).  A second warp arrives on it
+ * unless skip_arrive is non-zero; then the wait runs out, the kernel records DK_ERR_DEVICE_TIMEOUT
+ * (detail 0x7E57) in the device status word and returns -- the context stays usable.  No counterpart
+ * in the reference (its Triton kernels have no bounded waits). */
+int dk_test_bounded_wait(int skip_arrive, int64_t limit_ns, void* stream);
 
 /* ---- RMSNorm: y = x * rsqrt(mean(x^2) + eps) * w, f32 math, y in x's dtype ----
  * x, out: [n_rows, n_cols] with unit column stride and the given row strides
@@ -85,8 +91,8 @@ int dk_rmsnorm_batch_invariant(const void* x, int64_t x_row_stride, const void* 
 /* Embedding lookup + invariant RMSNorm: x_out[r, :] = table[row_index[r], :] and out[r, :] =
  * dk_rmsnorm_batch_invariant(x_out[r, :]), the same bits as the lookup followed by that call, in one
  * launch.  row_index: device int64[n_rows]; an index outside [0, table_rows) sets the device status
- * (DK_ERR_DEVICE_CHECK) and leaves its row unwritten.  Needs 16-byte aligned rows and n_cols a multiple
- * of 16 bytes (DK_ERR_UNSUPPORTED otherwise).  No counterpart in the reference: it fuses the decoder's
+ * (DK_ERR_DEVICE_CHECK) and leaves its row unwritten.  Any row alignment and n_cols (16-byte aligned rows
+ * with n_cols a multiple of 16 bytes take the vector path).  No counterpart in the reference: it fuses the decoder's
  * `self.embed[token_ids]` (kernels/tiny_model.py:110) into the first block's input norm. */
 int dk_rmsnorm_gather_batch_invariant(const void* table, int64_t table_row_stride, int64_t table_rows,
                                       const int64_t* row_index, const void* weight, void* x_out, int64_t x_row_stride,

@@ -1,8 +1,9 @@
 """Generate the golden fixtures in this directory from the REFERENCE's own code.
 
-Run here, where the reference checkout exists (it never runs on the GPU box):
+Run where a checkout of the reference exists (the path is an argument or
+$DETKERNELS_REFERENCE; nothing on the GPU side runs it):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path to the reference checkout>
 
 * rmsnorm / matmul / attention: the reference's eager ``*_reference`` functions
   (kernels/rmsnorm.py:39-48, kernels/matmul.py:42-49, kernels/attention.py:49-71)
@@ -128,4 +129,7 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DETKERNELS_REFERENCE")
+    if not ref:
+        sys.exit("usage: make_golden.py <reference checkout> (or set DETKERNELS_REFERENCE)")
+    main(ref)

@@ -159,3 +159,20 @@ def test_gather_equals_lookup_then_rmsnorm(dev, dtype_name, w_name):
     code, _ = _lib.device_status(torch.cuda.current_device(), clear=True)
     assert code == _lib.DK_ERR_DEVICE_CHECK
     assert torch.equal(x[0], table[3]) and int(x[1].count_nonzero()) == 0 and int(y[1].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("n_cols,offset", [(1001, 0), (12000, 0), (1024, 1)])
+def test_gather_scalar_path_equals_lookup_then_rmsnorm(dev, n_cols, offset):
+    """Rows the vector gather cannot take -- an odd hidden size, a row longer than the
+    vector kernel keeps in registers, an unaligned table view -- go through the scalar
+    gather, which walks the scalar RMSNorm's chunks: same bits as lookup + RMSNorm."""
+    import torch
+    from detkernels_b200.kernels.rmsnorm import rmsnorm_batch_invariant, rmsnorm_gather
+    g = torch.Generator(device=dev).manual_seed(5)
+    full = torch.randn(300, n_cols + offset, device=dev, generator=g).to(torch.bfloat16)
+    table = full[:, offset:]
+    w = (1.0 + 0.1 * torch.randn(n_cols, device=dev, generator=g)).to(torch.bfloat16)
+    idx = torch.randint(0, 300, (37,), device=dev, generator=g)
+    x, y = rmsnorm_gather(table, idx, w, 1e-6)
+    assert torch.equal(x, table[idx])
+    assert torch.equal(y, rmsnorm_batch_invariant(table[idx].contiguous(), w, 1e-6))

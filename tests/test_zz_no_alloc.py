@@ -76,9 +76,11 @@ def test_noalloc_rejects_calls_beyond_its_scratch(dev):
     lib = _lib.load()
     limit = lib.dk_attention_noalloc_scratch_limit()
     assert limit == 32 << 20
-    # 4096 rows x 8 kv heads x 32 splits x 4 rows x 130 floats is far beyond 32 MiB
+    # 4096 rows x 8 kv heads x 32 splits x 4 rows x 130 floats is far beyond 32 MiB; the cache
+    # really holds the 8192 tokens the call describes, so even a call that got past the size
+    # check would read only allocated memory
     q = torch.zeros(4096, 32, 128, device=dev, dtype=torch.bfloat16)
-    kc = torch.zeros(1, 8, 64, 128, device=dev, dtype=torch.bfloat16)
+    kc = torch.zeros(1, 8, 8192, 128, device=dev, dtype=torch.bfloat16)
     lens = torch.ones(4096, device=dev, dtype=torch.int32)
     out = torch.empty_like(q)
     rc = lib.dk_attention_batch_invariant_noalloc(
@@ -87,3 +89,26 @@ def test_noalloc_rejects_calls_beyond_its_scratch(dev):
         4096, 32, 8, 128, 8192, ctypes.c_float(0.088), _lib.DK_BF16, _lib.stream_ptr(q.device))
     assert rc == _lib.DK_ERR_WORKSPACE
     assert "built-in scratch" in _lib.last_error()
+
+
+def test_noalloc_clears_stale_counters_left_in_its_scratch(dev):
+    """A call that stopped early can leave non-zero arrival counters in the shared scratch.
+    Fill the start of the scratch with garbage through a test hook that is not part of the
+    public header, then check the next call still gives the workspace entry point's bits."""
+    import torch
+
+    from detkernels_b200 import _lib
+    from detkernels_b200.kernels.attention import attention_decode
+
+    lib = _lib.load()
+    fill = lib.dk_noalloc_scratch_fill_for_test
+    fill.restype = ctypes.c_int
+    fill.argtypes = [ctypes.c_int, ctypes.c_size_t]
+    for seed, B, H, Hkv, S, D in [(21, 5, 32, 8, 3000, 128), (22, 7, 16, 16, 900, 64)]:
+        q, kc, vc, lens = _case(dev, seed, B, H, Hkv, S, D)
+        want = attention_decode(q, kc, vc, lens, max_kv_len=S)
+        torch.cuda.synchronize()
+        _lib.check(fill(0x5A, 1 << 16), "dk_noalloc_scratch_fill_for_test")
+        got = _noalloc(q, kc, vc, lens, S)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), (seed, B, H, Hkv, S, D)
