@@ -348,6 +348,48 @@ def gemm_vs_cublas(iters=10):
     return res
 
 
+# ----------------------------------------------------------------------------- RMSNorm roofline
+RMS_ROWS = (4096, 65536)
+RMS_COLS = 4096
+
+
+def rmsnorm_roofline(peaks, iters=10):
+    """rmsnorm_batch_invariant on x f32 [B, 4096] for B in RMS_ROWS: achieved GB/s of the
+    algorithmic bytes 2*B*4096*4 + 4096*4 (read x and w, write y) against the measured HBM copy
+    peak.  B = 65536 moves 2.1 GB per call (no L2 reuse); B = 4096 (134 MB) flushes L2 first."""
+    import torch
+
+    from detkernels_b200.kernels.rmsnorm import rmsnorm_batch_invariant
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = 1 + 0.1 * torch.randn(RMS_COLS, device=dev, generator=g)
+    res = {}
+    for B in RMS_ROWS:
+        x = torch.randn(B, RMS_COLS, device=dev, generator=g)
+        out = rmsnorm_batch_invariant(x, w)
+        ts = []
+        for i in range(iters + 3):
+            if B * RMS_COLS * 4 < 2 * flush.numel():
+                flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            out = rmsnorm_batch_invariant(x, w)
+            e.record()
+            e.synchronize()
+            if i >= 3:
+                ts.append(s.elapsed_time(e))
+        ms = statistics.median(ts)
+        nbytes = 2 * B * RMS_COLS * 4 + RMS_COLS * 4
+        gbs = nbytes / ms / 1e6
+        res["B=%d" % B] = {"us": round(ms * 1e3, 2), "achieved_gbs": round(gbs, 1),
+                           "frac_hbm": round(gbs / peaks["hbm_gbs"], 4), "algorithmic_bytes": nbytes}
+        del x, out
+    del flush
+    return res
+
+
 # DRAM bytes (read + write) per algorithmic byte of the decode attention kernel, from an ncu
 # capture of `python -m detkernels_b200.kernels.benchmark` (B=64, H=8, S=2048, D=64: 270.21 MB
 # of DRAM traffic for 268.57 MB algorithmic); the kernel reads each KV byte once, so traffic
@@ -481,15 +523,29 @@ def run_ours(args, rank, world, local):
 
     dev = torch.device("cuda", local)
     model = TinyModel(TinyModelConfig(**MODEL), device=str(dev))
-    prompts = make_prompts(rank, BATCH_PER_GPU)
+    tp = args.tp
+    group = None
+    if tp > 1:
+        # tensor parallel: every rank serves the same 256 prompts with 1/tp of every layer
+        import torch.distributed as dist
+        if world != tp:
+            raise SystemExit("--tp %d needs %d ranks (torchrun --nproc-per-node %d), got %d" % (tp, tp, tp, world))
+        group = dist.group.WORLD
+        prompts = make_prompts(0, BATCH_PER_GPU)
+    else:
+        prompts = make_prompts(rank, BATCH_PER_GPU)
+    gen_kw = {"tp": tp, "group": group} if tp > 1 else {}
     cap = max(len(p) for p in prompts) + NEW_TOKENS
-    eng = model.engine(BATCH_PER_GPU, max(cap, OTHER_LEN[1] + NEW_TOKENS))
+    if tp > 1:
+        eng = model.tp_engine(tp, BATCH_PER_GPU, max(cap, OTHER_LEN[1] + NEW_TOKENS), group)
+    else:
+        eng = model.engine(BATCH_PER_GPU, max(cap, OTHER_LEN[1] + NEW_TOKENS))
     plan = eng.plan(prompts)
 
-    # solo reference for the tracked prompt (divergence check)
+    # solo reference for the tracked prompt (divergence check); a TP solo run is collective
     solo = None
-    if rank == 0:
-        solo = model.generate([prompts[0]], NEW_TOKENS, "batch_invariant")[0].clone()
+    if rank == 0 or tp > 1:
+        solo = model.generate([prompts[0]], NEW_TOKENS, "batch_invariant", **gen_kw)[0].clone()
 
     for _ in range(args.warmup):
         eng.run(plan, NEW_TOKENS, timing=False)
@@ -533,7 +589,9 @@ def run_ours(args, rank, world, local):
     ms_total = start.elapsed_time(end)
     ms_max = max_over_ranks(ms_total, world)
     ms_per_step = ms_max / args.steps
-    tokens_all = sum_over_ranks(float(len(prompts) * NEW_TOKENS * args.steps), world)
+    tokens_all = float(len(prompts) * NEW_TOKENS * args.steps)
+    if tp == 1:
+        tokens_all = sum_over_ranks(tokens_all, world)
     value = tokens_all / (ms_max / 1e3)
 
     # divergences: tracked row identical in every timed step and to its solo run
@@ -545,7 +603,7 @@ def run_ours(args, rank, world, local):
 
     # ---- end-to-end through the public API with host buffers ----
     for _ in range(0 if args.skip_e2e else 2):   # warm the public path (graph captured on first use)
-        model.generate(prompts, NEW_TOKENS, "batch_invariant").cpu()
+        model.generate(prompts, NEW_TOKENS, "batch_invariant", **gen_kw).cpu()
     barrier(world)
     torch.cuda.synchronize(dev)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -553,7 +611,7 @@ def run_ours(args, rank, world, local):
     d2h = 0
     e_start.record()
     for _ in range(0 if args.skip_e2e else args.steps):
-        res = model.generate(prompts, NEW_TOKENS, "batch_invariant")
+        res = model.generate(prompts, NEW_TOKENS, "batch_invariant", **gen_kw)
         host = res.cpu()
         d2h = host.numel() * host.element_size()
     e_end.record()
@@ -562,6 +620,12 @@ def run_ours(args, rank, world, local):
     h2d = eng.plan(prompts)["h2d_bytes"]
     e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
     e2e_value = None if args.skip_e2e else tokens_all / (e2e_ms / 1e3)
+    if tp > 1:
+        # CUDA graphs that hold NCCL calls go before the process group does
+        del eng
+        model._engines.clear()
+        torch.cuda.synchronize(dev)
+        barrier(world)
 
     if rank != 0:
         return 0
@@ -569,7 +633,7 @@ def run_ours(args, rank, world, local):
     # ---- roofline of the dominant kernel (decode attention, HBM bound) ----
     peaks, peak_kind = load_peaks()
     lens = np.array([len(p) for p in prompts], dtype=np.int64)
-    H, D = MODEL["num_heads"], MODEL["head_dim"]
+    H, D = MODEL["num_heads"] // tp, MODEL["head_dim"]     # one rank's heads
     steps_dec = NEW_TOKENS - 1
     kv_bytes = 0
     for t in range(steps_dec):
@@ -596,15 +660,18 @@ def run_ours(args, rank, world, local):
         parity = {"oracle_token_match": float((ours_small == cpu_toks).mean()),
                   "tracked_prefix_match": int(np.argmin(np.append(ours_small[0] == cpu_toks[0], False)))}
 
-    gemm = gemm_vs_cublas() if not args.skip_gemm else None
-    gdn = gdn_bench(peaks) if not args.skip_gdn and rank == 0 else None
+    gemm = gemm_vs_cublas() if not args.skip_gemm and world == 1 else None
+    rms = rmsnorm_roofline(peaks) if world == 1 else None
+    gdn = gdn_bench(peaks) if not args.skip_gdn and world == 1 else None
 
     line = {
         "metric": "BI decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong" if tp > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random prompts, random-init weights)",
-        "config": workload_config(world), "parallelism": "dp%d (request-sharded, no collective)" % world,
+        "config": workload_config(1 if tp > 1 else world),
+        "parallelism": ("tp%d (every layer split over %d ranks, NCCL all-gather of f32 slice sums)" % (tp, tp)
+                        if tp > 1 else "dp%d (request-sharded, no collective)" % world),
         "e2e": {"value": e2e_value and round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),
@@ -614,6 +681,7 @@ def run_ours(args, rank, world, local):
         "divergences": divergences,
         "parity": parity,
         "gemm_vs_cublas": gemm,
+        "rmsnorm_roofline": rms,
         "gdn": gdn,
     }
     print(json.dumps(line), flush=True)
@@ -632,13 +700,19 @@ def main(argv=None):
     ap.add_argument("--skip-e2e", action="store_true", help="skip the end-to-end public-API timing")
     ap.add_argument("--skip-gdn", action="store_true", help="skip the gated-delta-rule section")
     ap.add_argument("--gdn-only", action="store_true", help="run and print only the gated-delta-rule section")
+    ap.add_argument("--rmsnorm-only", action="store_true", help="run and print only the RMSNorm roofline section")
+    ap.add_argument("--tp", type=int, default=1, choices=[1, 2, 4, 8],
+                    help="tensor-parallel decode over the torchrun ranks (needs --nproc-per-node TP)")
     ap.add_argument("--new-tokens", type=int, default=NEW_TOKENS,
                     help="tokens generated per prompt (the workload is 128; smaller only for profiling)")
     args = ap.parse_args(argv)
     NEW_TOKENS = args.new_tokens
-    if args.gdn_only:
+    if args.gdn_only or args.rmsnorm_only:
+        import torch
+        torch.cuda.set_device(0)
         peaks, _ = load_peaks()
-        print(json.dumps({"gdn": gdn_bench(peaks)}), flush=True)
+        section = {"gdn": gdn_bench(peaks)} if args.gdn_only else {"rmsnorm_roofline": rmsnorm_roofline(peaks)}
+        print(json.dumps(section), flush=True)
         return 0
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))

@@ -60,6 +60,9 @@ SIGNATURES = {
                               _int, _int, _int, _int, _int, _int, ctypes.c_float, _c_void_p, _int, _c_void_p, _int,
                               _c_void_p]),
     "dk_argmax_finish": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "dk_matmul_fold_slices_ex": (_int, [_c_void_p, _int, _c_void_p, _i64, _i64, _i64, _int, _c_void_p, _c_void_p]),
+    "dk_argmax_finish_parts": (_int, [_c_void_p, _int, _i64, ctypes.POINTER(_i64), _i64, _c_void_p, _c_void_p,
+                                      _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "dk_matmul_shard_range": (None, [_i64, _int, _int, _c_void_p, _c_void_p]),
     "dk_matmul_shard_partials": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _int, _int,
                                         _int, _c_void_p]),

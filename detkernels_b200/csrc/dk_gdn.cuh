@@ -42,7 +42,7 @@ struct Params {
   const void* beta;   // [tokens, HV]
   void* o;            // [tokens, HV, DV], q's dtype
   const int64_t* cu_seqlens;  // device [n_seq + 1] or null (then sequence n = tokens [n*T, (n+1)*T))
-  int64_t seq_len;            // T when cu_seqlens is null
+  int64_t seq_len;            // T when cu_seqlens is null; else the packed length (bound of cu_seqlens)
   const void* h0;             // [n_seq, HV, DK, DV] or null (zeros)
   float* ht;                  // [n_seq, HV, DK, DV] f32 or null
   int H, HV;
@@ -51,6 +51,26 @@ struct Params {
   int chunk;                  // tokens per chunk: 64 (chunked) or 1 (token-by-token recurrence)
   float scale;
 };
+
+// Token range [bos, bos + len) of sequence n.  With cu_seqlens, p.seq_len holds the packed length
+// and a pair outside [0, seq_len] or decreasing is recorded as DK_ERR_DEVICE_CHECK (detail 0x500)
+// and the CTA skips the sequence (every thread of the CTA takes the same branch), so a bad
+// cu_seqlens never makes a kernel read or write outside the caller's buffers.
+__device__ __forceinline__ bool seq_range(const Params& p, int n, int64_t& bos, int64_t& len) {
+  if (p.cu_seqlens) {
+    const int64_t b = p.cu_seqlens[n], e = p.cu_seqlens[n + 1];
+    if (b < 0 || e < b || e > p.seq_len) {
+      if (threadIdx.x == 0) report_error(DK_ERR_DEVICE_CHECK, 0x500);
+      return false;
+    }
+    bos = b;
+    len = e - b;
+  } else {
+    bos = static_cast<int64_t>(n) * p.seq_len;
+    len = p.seq_len;
+  }
+  return true;
+}
 
 __device__ __forceinline__ float load_any(const void* p, int64_t i, int dtype) {
   if (dtype == DK_F32) return static_cast<const float*>(p)[i];
@@ -95,13 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(const Params p) 
   const int hq = hv / (HV / p.H);
   const int tid = threadIdx.x;
   int64_t bos, len;
-  if (p.cu_seqlens) {
-    bos = p.cu_seqlens[n];
-    len = p.cu_seqlens[n + 1] - bos;
-  } else {
-    bos = static_cast<int64_t>(n) * p.seq_len;
-    len = p.seq_len;
-  }
+  if (!seq_range(p, n, bos, len)) return;
   const T* q = static_cast<const T*>(p.q);
   const T* k = static_cast<const T*>(p.k);
   const T* v = static_cast<const T*>(p.v);
@@ -348,13 +362,7 @@ __global__ void __launch_bounds__(32 * kRecWarps) gdn_recurrent_kernel(const Par
   const int c = blockIdx.z * 32 + lane;
   const int row0 = warp * kRows;
   int64_t bos, len;
-  if (p.cu_seqlens) {
-    bos = p.cu_seqlens[n];
-    len = p.cu_seqlens[n + 1] - bos;
-  } else {
-    bos = static_cast<int64_t>(n) * p.seq_len;
-    len = p.seq_len;
-  }
+  if (!seq_range(p, n, bos, len)) return;
   const T* q = static_cast<const T*>(p.q);
   const T* k = static_cast<const T*>(p.k);
   const T* v = static_cast<const T*>(p.v);

@@ -146,13 +146,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gdn_chunk_tc_kernel(const Param
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t4 = lane & 3;
   int64_t bos, len;
-  if (p.cu_seqlens) {
-    bos = p.cu_seqlens[n];
-    len = p.cu_seqlens[n + 1] - bos;
-  } else {
-    bos = static_cast<int64_t>(n) * p.seq_len;
-    len = p.seq_len;
-  }
+  if (!seq_range(p, n, bos, len)) return;
   const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(p.q);
   const __nv_bfloat16* k = static_cast<const __nv_bfloat16*>(p.k);
   const __nv_bfloat16* v = static_cast<const __nv_bfloat16*>(p.v);

@@ -870,6 +870,37 @@ __global__ void argmax_finish_kernel(unsigned long long* __restrict__ keys, int6
   }
 }
 
+// Column offsets of the parts of a column-parallel argmax (at most 8 tensor-parallel ranks).
+struct PartOffsets {
+  int64_t v[8];
+};
+
+// Cross-part argmax: part p's keys (local column indices) become global by subtracting
+// offsets.v[p] from the key (its low word is ~column), the largest key over the parts wins
+// (largest value, then smallest global column), then as argmax_finish_kernel.
+__global__ void argmax_finish_parts_kernel(const unsigned long long* __restrict__ keys, int n_parts,
+                                           int64_t part_stride, PartOffsets offs, int64_t n_rows, int64_t* tokens,
+                                           int64_t* tokens_copy, int32_t* lens_a, int32_t* lens_b,
+                                           unsigned long long* reset_keys) {
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < n_rows;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    unsigned long long best = 0ull;
+    for (int q = 0; q < n_parts; ++q) {
+      unsigned long long k = keys[q * part_stride + r];
+      if (k != 0ull) k -= static_cast<unsigned long long>(offs.v[q]);
+      best = k > best ? k : best;
+    }
+    const int64_t col = static_cast<int64_t>(~static_cast<uint32_t>(best & 0xffffffffull));
+    tokens[r] = col;
+    if (tokens_copy) tokens_copy[r] = col;
+    if (reset_keys) reset_keys[r] = 0ull;
+    if (lens_a) lens_a[r] += 1;
+    if (lens_b) lens_b[r] += 1;
+  }
+}
+
 // f32 [M][N] -> output dtype (batch-variant twin's final cast).
 template <typename T>
 __global__ void cast_out_kernel(const float* __restrict__ src, T* __restrict__ c, int64_t ldc, int M, int N) {

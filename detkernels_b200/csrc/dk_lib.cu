@@ -896,6 +896,80 @@ int dk_matmul_fold_slices(const float* partials, int n_parts, void* c, int64_t l
   return launch_fold<__half>(partials, n_parts, p, st);
 }
 
+int dk_matmul_fold_slices_ex(const float* partials, int n_parts, void* c, int64_t ldc, int64_t M, int64_t N,
+                             int dtype, const dk_matmul_epilogue* epi, void* stream) {
+  const char* what = "matmul_fold_slices_ex";
+  if (dtype != DK_BF16 && dtype != DK_F16) return fail(DK_ERR_UNSUPPORTED, "%s: bad dtype", what);
+  if (n_parts != 1 && n_parts != 2 && n_parts != 4 && n_parts != 8)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: n_parts must be 1, 2, 4 or 8", what);
+  if (M < 0 || N < 0 || M > 0x7fffffffLL || N > 0x7fffffffLL) return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad shape", what);
+  if (M == 0 || N == 0) return DK_OK;
+  if (!partials) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null partials", what);
+  dk_matmul_epilogue e{};
+  e.mode = DK_EPI_STORE;
+  if (epi) e = *epi;
+  int64_t out_cols = N;
+  switch (e.mode) {
+    case DK_EPI_STORE:
+    case DK_EPI_SILU:
+      break;
+    case DK_EPI_RESIDUAL:
+    case DK_EPI_RESIDUAL_RMSNORM:
+      if (!e.resid || e.ld_resid < N) return fail(DK_ERR_INVALID_ARGUMENT, "%s: residual epilogue needs R", what);
+      if (e.mode == DK_EPI_RESIDUAL_RMSNORM && (!e.norm_w || !e.norm_out || e.norm_ld < N || !valid_dtype(e.norm_w_dtype)))
+        return fail(DK_ERR_INVALID_ARGUMENT, "%s: RMSNorm epilogue needs a weight, an output and norm_ld >= N", what);
+      break;
+    case DK_EPI_SILU_MUL:
+      if (N % 2) return fail(DK_ERR_INVALID_ARGUMENT, "%s: gate/up epilogue needs an even N", what);
+      out_cols = N / 2;
+      break;
+    case DK_EPI_ARGMAX:
+      if (!e.argmax_keys) return fail(DK_ERR_INVALID_ARGUMENT, "%s: argmax epilogue needs keys", what);
+      if (!c) out_cols = 0;
+      break;
+    default:
+      return fail(DK_ERR_UNSUPPORTED, "%s: epilogue mode %d is not available after a fold", what, e.mode);
+  }
+  if (out_cols > 0 && (!c || ldc < out_cols)) return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad output or ldc", what);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  dk::gemm::Params p{};
+  p.epi = e;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.c = c;
+  p.ldc = ldc;
+  if (e.mode == DK_EPI_RESIDUAL_RMSNORM) {
+    const NormSpec nm{e.norm_w, e.norm_w_dtype, e.norm_out, e.norm_ld, e.norm_eps};
+    p.epi.mode = DK_EPI_RESIDUAL;
+    return launch_fold_norm(dtype, partials, n_parts, p, nm, st);
+  }
+  if (dtype == DK_BF16) return launch_fold<__nv_bfloat16>(partials, n_parts, p, st);
+  return launch_fold<__half>(partials, n_parts, p, st);
+}
+
+int dk_argmax_finish_parts(const unsigned long long* keys, int n_parts, int64_t part_stride,
+                           const int64_t* col_offsets, int64_t n_rows, int64_t* tokens, int64_t* tokens_copy,
+                           int32_t* lens_a, int32_t* lens_b, unsigned long long* reset_keys, void* stream) {
+  const char* what = "argmax_finish_parts";
+  if (n_rows < 0 || n_parts < 1 || n_parts > 8 || part_stride < n_rows)
+    return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad sizes (1 <= n_parts <= 8, part_stride >= n_rows)", what);
+  if (n_rows == 0) return DK_OK;
+  if (!keys || !tokens || !col_offsets) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null keys, tokens or offsets", what);
+  dk::gemm::PartOffsets offs{};
+  for (int q = 0; q < n_parts; ++q) {
+    if (col_offsets[q] < 0 || col_offsets[q] > 0x7fffffffLL)
+      return fail(DK_ERR_INVALID_ARGUMENT, "%s: column offset out of range", what);
+    offs.v[q] = col_offsets[q];
+  }
+  const int64_t want = ceil_div(n_rows, 256);
+  const int blocks = static_cast<int>(want < 1024 ? want : 1024);
+  cudaError_t e = launch_pdl(dk::gemm::argmax_finish_parts_kernel, dim3(blocks), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), keys, n_parts, part_stride, offs, n_rows, tokens,
+                             tokens_copy, lens_a, lens_b, reset_keys);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return DK_OK;
+}
+
 int dk_matmul_batch_variant(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc, int64_t M,
                             int64_t N, int64_t K, int dtype, int split_m_threshold, int split_k, void* workspace,
                             size_t workspace_bytes, void* stream) {

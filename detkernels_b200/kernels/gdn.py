@@ -59,9 +59,18 @@ def _forward(q, k, v, g, beta, scale, initial_state, output_final_state, cu_seql
         if B != 1:
             raise ValueError("The batch size is expected to be 1 rather than %d when using `cu_seqlens`."
                              "Please flatten variable-length inputs before processing." % B)
+        if cu_seqlens.dim() != 1 or cu_seqlens.numel() < 1:
+            raise ValueError("cu_seqlens must be a 1-D tensor of N + 1 offsets")
+        if not cu_seqlens.is_cuda:
+            # host offsets are checked here; device offsets are checked by the kernels, which skip
+            # a bad sequence and record DK_ERR_DEVICE_CHECK instead of reading outside the inputs
+            host = cu_seqlens.to(torch.int64)
+            if bool((host < 0).any()) or bool((host[1:] < host[:-1]).any()) or int(host[-1]) > T:
+                raise ValueError("cu_seqlens must be non-decreasing offsets within [0, T=%d], got %s"
+                                 % (T, host.tolist()))
         cu = cu_seqlens.to(device=q.device, dtype=torch.int64).contiguous()
         N = cu.numel() - 1
-        seq_len = 0
+        seq_len = T   # the packed length: the bound the kernels check cu_seqlens against
     else:
         cu = None
         N = B

@@ -178,43 +178,8 @@ def matmul_fused(a, b, epilogue: str = "store", out=None, workspace=None, residu
     import torch
 
     M, K, N = _check_inputs(a, b, "matmul_fused")
-    if epilogue not in _EPILOGUES:
-        raise ValueError("unknown epilogue %r" % (epilogue,))
-    epi = _lib.MatmulEpilogue()
-    epi.mode = _EPILOGUES[epilogue]
-    out_cols = N
-    if epilogue in ("residual", "residual_rmsnorm"):
-        assert residual is not None and residual.shape == (M, N) and residual.dtype == a.dtype
-        assert residual.is_cuda and residual.stride(1) == 1
-        epi.resid, epi.ld_resid = residual.data_ptr(), residual.stride(0)
-        if epilogue == "residual_rmsnorm":
-            assert norm_weight is not None and norm_weight.is_cuda and norm_weight.is_contiguous()
-            assert norm_weight.numel() == N
-            assert norm_out is not None and norm_out.shape == (M, N) and norm_out.dtype == a.dtype
-            assert norm_out.stride(1) == 1
-            epi.norm_w, epi.norm_w_dtype = norm_weight.data_ptr(), _lib.dtype_code(norm_weight.dtype)
-            epi.norm_out, epi.norm_ld, epi.norm_eps = norm_out.data_ptr(), norm_out.stride(0), float(eps)
-    elif epilogue == "silu_mul":
-        if N % 2:
-            raise ValueError("silu_mul needs an even number of columns")
-        out_cols = N // 2
-    elif epilogue == "qkv_cache":
-        kv_cols = (N - q_cols) // 2
-        assert k_cache is not None and v_cache is not None and row_pos is not None
-        assert k_cache.shape == v_cache.shape and k_cache.stride() == v_cache.stride()
-        assert k_cache.dtype == a.dtype and k_cache.stride(3) == 1 and k_cache.shape[3] == head_dim
-        assert row_pos.dtype == torch.int32 and row_pos.numel() >= M
-        assert row_seq is None or (row_seq.dtype == torch.int32 and row_seq.numel() >= M)
-        epi.q_cols, epi.kv_cols, epi.head_dim = int(q_cols), int(kv_cols), int(head_dim)
-        epi.k_cache, epi.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
-        epi.cache_stride_seq, epi.cache_stride_head, epi.cache_stride_tok = k_cache.stride(0), k_cache.stride(1), \
-            k_cache.stride(2)
-        epi.row_seq = row_seq.data_ptr() if row_seq is not None else None
-        epi.row_pos = row_pos.data_ptr()
-        out_cols = q_cols
-    elif epilogue == "argmax":
-        assert argmax_keys is not None and argmax_keys.dtype == torch.int64 and argmax_keys.numel() >= M
-        epi.argmax_keys = argmax_keys.data_ptr()
+    epi, out_cols = _epilogue_struct(epilogue, M, N, a.dtype, residual, q_cols, head_dim, k_cache, v_cache, row_seq,
+                                     row_pos, argmax_keys, norm_weight, norm_out, eps)
     if out is None and epilogue != "argmax":
         out = torch.empty((M, out_cols), device=a.device, dtype=a.dtype)
     if out is not None:
@@ -236,6 +201,82 @@ def matmul_fused(a, b, epilogue: str = "store", out=None, workspace=None, residu
     return out
 
 
+def _epilogue_struct(epilogue, M, N, dtype, residual=None, q_cols=0, head_dim=0, k_cache=None, v_cache=None,
+                     row_seq=None, row_pos=None, argmax_keys=None, norm_weight=None, norm_out=None, eps=1e-6):
+    """(dk_matmul_epilogue, output columns) for an [M, N] product of ``dtype`` with ``epilogue``."""
+    import torch
+
+    if epilogue not in _EPILOGUES:
+        raise ValueError("unknown epilogue %r" % (epilogue,))
+    epi = _lib.MatmulEpilogue()
+    epi.mode = _EPILOGUES[epilogue]
+    out_cols = N
+    if epilogue in ("residual", "residual_rmsnorm"):
+        assert residual is not None and residual.shape == (M, N) and residual.dtype == dtype
+        assert residual.is_cuda and residual.stride(1) == 1
+        epi.resid, epi.ld_resid = residual.data_ptr(), residual.stride(0)
+        if epilogue == "residual_rmsnorm":
+            assert norm_weight is not None and norm_weight.is_cuda and norm_weight.is_contiguous()
+            assert norm_weight.numel() == N
+            assert norm_out is not None and norm_out.shape == (M, N) and norm_out.dtype == dtype
+            assert norm_out.stride(1) == 1
+            epi.norm_w, epi.norm_w_dtype = norm_weight.data_ptr(), _lib.dtype_code(norm_weight.dtype)
+            epi.norm_out, epi.norm_ld, epi.norm_eps = norm_out.data_ptr(), norm_out.stride(0), float(eps)
+    elif epilogue == "silu_mul":
+        if N % 2:
+            raise ValueError("silu_mul needs an even number of columns")
+        out_cols = N // 2
+    elif epilogue == "qkv_cache":
+        kv_cols = (N - q_cols) // 2
+        assert k_cache is not None and v_cache is not None and row_pos is not None
+        assert k_cache.shape == v_cache.shape and k_cache.stride() == v_cache.stride()
+        assert k_cache.dtype == dtype and k_cache.stride(3) == 1 and k_cache.shape[3] == head_dim
+        assert row_pos.dtype == torch.int32 and row_pos.numel() >= M
+        assert row_seq is None or (row_seq.dtype == torch.int32 and row_seq.numel() >= M)
+        epi.q_cols, epi.kv_cols, epi.head_dim = int(q_cols), int(kv_cols), int(head_dim)
+        epi.k_cache, epi.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+        epi.cache_stride_seq, epi.cache_stride_head, epi.cache_stride_tok = k_cache.stride(0), k_cache.stride(1), \
+            k_cache.stride(2)
+        epi.row_seq = row_seq.data_ptr() if row_seq is not None else None
+        epi.row_pos = row_pos.data_ptr()
+        out_cols = q_cols
+    elif epilogue == "argmax":
+        assert argmax_keys is not None and argmax_keys.dtype == torch.int64 and argmax_keys.numel() >= M
+        epi.argmax_keys = argmax_keys.data_ptr()
+    return epi, out_cols
+
+
+def matmul_fold_fused(partials, dtype, epilogue: str = "store", out=None, residual=None, argmax_keys=None,
+                      norm_weight=None, norm_out=None, eps: float = 1e-6):
+    """``matmul_fold_slices`` followed by a fused epilogue (``"store"``, ``"residual"``,
+    ``"residual_rmsnorm"``, ``"silu"``, ``"silu_mul"`` or ``"argmax"``), applied as
+    ``matmul_fused`` applies it: a row-parallel layer whose ranks' subtree sums were gathered
+    gets the one-GPU fused layer's bits."""
+    import ctypes
+
+    import torch
+
+    assert partials.is_cuda and partials.dtype == torch.float32 and partials.is_contiguous()
+    n_parts, M, N = partials.shape
+    if epilogue == "qkv_cache":
+        raise ValueError("the qkv_cache epilogue is not available after a fold")
+    epi, out_cols = _epilogue_struct(epilogue, M, N, dtype, residual, argmax_keys=argmax_keys,
+                                     norm_weight=norm_weight, norm_out=norm_out, eps=eps)
+    if out is None and epilogue != "argmax":
+        out = torch.empty((M, out_cols), device=partials.device, dtype=dtype)
+    if out is not None:
+        assert out.shape == (M, out_cols) and out.dtype == dtype and out.stride(1) == 1
+    if M == 0 or N == 0:
+        return out
+    rc = _lib.load().dk_matmul_fold_slices_ex(
+        partials.data_ptr(), int(n_parts), out.data_ptr() if out is not None else None,
+        out.stride(0) if out is not None else out_cols, M, N, _lib.dtype_code(dtype), ctypes.byref(epi),
+        _lib.stream_ptr(partials.device))
+    _lib.check(rc, "matmul_fold_fused")
+    _lib.count_launch()
+    return out
+
+
 def argmax_finish(argmax_keys, tokens, tokens_copy=None, lens_a=None, lens_b=None):
     """After an ``"argmax"`` matmul over n rows: tokens[r] (int64) = row r's argmax column (also
     into tokens_copy), keys re-zeroed, lens_a/lens_b (int32) advanced by one."""
@@ -251,5 +292,32 @@ def argmax_finish(argmax_keys, tokens, tokens_copy=None, lens_a=None, lens_b=Non
         lens_a.data_ptr() if lens_a is not None else None, lens_b.data_ptr() if lens_b is not None else None,
         _lib.stream_ptr(tokens.device))
     _lib.check(rc, "argmax_finish")
+    _lib.count_launch()
+    return tokens
+
+
+def argmax_finish_parts(gathered_keys, col_offsets, tokens, tokens_copy=None, lens_a=None, lens_b=None,
+                        reset_keys=None):
+    """End of a greedy step for a column-parallel LM head: gathered_keys [n_parts, n] (int64 used as
+    uint64) hold each part's ``"argmax"`` keys over its own columns, which start at col_offsets[p] of
+    the vocabulary.  tokens[r] = the global argmax (the one-GPU answer); tokens_copy, lens and
+    reset_keys as in ``argmax_finish``."""
+    import ctypes
+
+    import torch
+
+    n_parts, n = gathered_keys.shape
+    assert gathered_keys.dtype == torch.int64 and gathered_keys.is_contiguous() and gathered_keys.is_cuda
+    assert len(col_offsets) == n_parts and tokens.dtype == torch.int64 and tokens.numel() >= n
+    for t in (lens_a, lens_b):
+        assert t is None or (t.dtype == torch.int32 and t.numel() >= n)
+    for t in (tokens_copy, reset_keys):
+        assert t is None or (t.dtype == torch.int64 and t.numel() >= n)
+    offs = (ctypes.c_int64 * n_parts)(*[int(o) for o in col_offsets])
+    ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+    rc = _lib.load().dk_argmax_finish_parts(
+        gathered_keys.data_ptr(), int(n_parts), n, offs, n, tokens.data_ptr(), ptr(tokens_copy), ptr(lens_a),
+        ptr(lens_b), ptr(reset_keys), _lib.stream_ptr(tokens.device))
+    _lib.check(rc, "argmax_finish_parts")
     _lib.count_launch()
     return tokens

@@ -183,13 +183,24 @@ class TinyModel:
         logits = matmul(rmsnorm(x, self.norm_f_w, cfg.eps), self.w_lm_head)
         return logits, new_kv_cache
 
-    def generate(self, prompt_token_ids, n_steps: int, kernel_set: str):
+    def generate(self, prompt_token_ids, n_steps: int, kernel_set: str, *, tp: int = 1, group=None):
         """Greedy decoding.  prompt_token_ids: (B,) int64 start tokens (the
         reference's form) or a list of B token-id lists (ragged prompts).
-        Returns (B, n_steps) generated token ids."""
+        Returns (B, n_steps) generated token ids.
+
+        tp / group (keyword-only, invariant kernel set on CUDA): decode with every layer split
+        over ``tp`` tensor-parallel ranks -- the ranks of ``group`` (a torch.distributed group of
+        ``tp`` processes, each calling generate with the same prompts), or, with ``group=None``,
+        all ``tp`` ranks in this process on this model's GPU.  The tokens equal TP=1's bit for bit."""
         import torch
 
         ragged = isinstance(prompt_token_ids, (list, tuple))
+        if tp != 1 or group is not None:
+            if kernel_set != "batch_invariant" or not str(self.device).startswith("cuda"):
+                raise ValueError("tensor-parallel decoding runs the batch_invariant kernel set on CUDA")
+            prompts = (list(prompt_token_ids) if ragged else [[int(t)] for t in prompt_token_ids.tolist()])
+            cap = max(len(p) for p in prompts) + n_steps
+            return self.tp_engine(tp, len(prompts), cap, group).generate(prompts, n_steps)
         if kernel_set == "batch_invariant" and str(self.device).startswith("cuda"):
             # ragged prompts go to the engine as given (any int sequence; the plan reads them
             # with numpy); a (B,) tensor becomes B one-token prompts
@@ -229,13 +240,25 @@ class TinyModel:
             outs.append(torch.cat(seq))
         return torch.stack(outs)
 
+    def tp_engine(self, tp: int, max_batch: int, max_seq_len: int, group=None, use_graph: bool = True):
+        """A cached tensor-parallel engine (see ``tp_model.TPDecodeEngine``)."""
+        from .tp_model import TPDecodeEngine
+
+        gid = id(group) if group is not None else None
+        for (kind, t, g_id, b, s, g), eng in self._engines.items():
+            if kind == "tp" and t == tp and g_id == gid and b >= max_batch and s >= max_seq_len and g == use_graph:
+                return eng
+        eng = TPDecodeEngine(self, tp, max_batch, max_seq_len, group=group, use_graph=use_graph)
+        self._engines[("tp", tp, gid, max_batch, max_seq_len, use_graph)] = eng
+        return eng
+
     def engine(self, max_batch: int, max_seq_len: int, use_graph: bool = True) -> "DecodeEngine":
         """A cached DecodeEngine whose capacity covers (max_batch, max_seq_len)."""
-        for (b, s, g), eng in self._engines.items():
-            if b >= max_batch and s >= max_seq_len and g == use_graph:
+        for (kind, _, _, b, s, g), eng in self._engines.items():
+            if kind == "dp" and b >= max_batch and s >= max_seq_len and g == use_graph:
                 return eng
         eng = DecodeEngine(self, max_batch, max_seq_len, use_graph=use_graph)
-        self._engines[(max_batch, max_seq_len, use_graph)] = eng
+        self._engines[("dp", 1, None, max_batch, max_seq_len, use_graph)] = eng
         return eng
 
 
@@ -247,6 +270,8 @@ class DecodeEngine:
     op is per-row, prefill rows of one sequence share attention tiles that
     reproduce decode-row bits, and the decode graph has a fixed shape (rows
     beyond the live batch are computed and ignored)."""
+
+    MAX_GRAPHS = 8   # captured decode graphs kept per engine
 
     def __init__(self, model: TinyModel, max_batch: int, max_seq_len: int, use_graph: bool = True):
         import torch
@@ -373,9 +398,10 @@ class DecodeEngine:
         lib = self._lib.load()
         R = host["tok"].numel()
         a_ws = lib.dk_attention_workspace_size(len(tiles), 2, self.H, self.Hkv, self.D, plan["max_len"])
-        g_ws = max(lib.dk_matmul_workspace_size(R, n, k) for (n, k) in [
+        g_ws = max([lib.dk_matmul_workspace_size(R, n, k) for (n, k) in [
             ((self.H + 2 * self.Hkv) * self.D, self.h), (self.h, self.h), (self.h, self.cfg.mlp_hidden),
-            (2 * self.cfg.mlp_hidden, self.h), (self.cfg.mlp_hidden, self.h)])
+            (2 * self.cfg.mlp_hidden, self.h), (self.cfg.mlp_hidden, self.h)]] +
+            [lib.dk_matmul_workspace_size(B, self._head_cols(), self.h)])   # the LM head on B last rows
         plan["attn_ws"] = torch.zeros(max(a_ws, 1), dtype=torch.uint8, device=dev)
         plan["gemm_ws"] = torch.zeros(max(g_ws, 1), dtype=torch.uint8, device=dev)
         return plan
@@ -397,6 +423,14 @@ class DecodeEngine:
         self.kv_lens[:plan["B"]] = plan["lens"]
         self.q_lens.copy_(self.kv_lens + 1)
         return logits
+
+    def _head_cols(self):
+        """Columns of the LM head matmul this engine runs."""
+        return self.cfg.vocab_size
+
+    def _prefill_tokens(self, plan):
+        """Greedy first token of each prompt (device int64 [B])."""
+        return self.prefill(plan).argmax(dim=-1)
 
     # ---------------- decode ----------------
     def _decode_step(self, max_len, out_row=None, events=None):
@@ -452,6 +486,9 @@ class DecodeEngine:
             return torch.empty((0, self.B), dtype=torch.long, device=self.device)
         if start_len is None:
             start_len = self.S - n_steps
+        # the bound only sizes the attention grid (a row's bits follow its own length), so it is
+        # rounded up to the 256-token KV split: batches of similar lengths share a captured graph
+        start_len = min(-(-int(start_len) // 256) * 256, self.S - n_steps)
         if not self.use_graph:
             out = torch.empty((n_steps, self.B), dtype=torch.long, device=self.device)
             for t in range(n_steps):
@@ -459,6 +496,8 @@ class DecodeEngine:
             return out
         key = (n_steps, start_len, timing)
         if key not in self._graphs:
+            while len(self._graphs) >= self.MAX_GRAPHS:     # oldest capture first
+                self._graphs.pop(next(iter(self._graphs)))
             self._graphs[key] = self._capture(n_steps, start_len, timing)
         g, out, events, n_graph = self._graphs[key]
         g.replay()
@@ -486,7 +525,7 @@ class DecodeEngine:
             return torch.empty((B, 0), dtype=torch.long, device=self.device)
         if plan["max_len"] + n_steps > self.S:
             raise ValueError("prompt + n_steps exceeds the engine's max_seq_len")
-        first = self.prefill(plan).argmax(dim=-1)
+        first = self._prefill_tokens(plan)
         self.tokens.zero_()
         self.tokens[:B] = first
         if before_decode is not None:

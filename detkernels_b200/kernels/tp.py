@@ -87,6 +87,20 @@ def _fold(gathered, dtype):
     return matmul_fold_slices(gathered, dtype)
 
 
+def check_agreement(group=None, **fields):
+    """Every rank of ``group`` must pass equal ``fields`` (TP size, shard counts, shapes ...):
+    one all_gather_object, then ValueError on every rank if any rank differs, so a rank with a
+    different split fails before its first data exchange instead of hanging it."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    got = [None] * world
+    dist.all_gather_object(got, fields, group=group)
+    if any(g != got[0] for g in got):
+        raise ValueError("tensor-parallel ranks disagree: %s" % got)
+    return got[0]
+
+
 def all_gather_ranks(t, group=None):
     """[world, *t.shape] stack of every rank's tensor, in rank order."""
     import torch

@@ -202,6 +202,22 @@ int dk_matmul_batch_invariant_ex(const void* a, int64_t lda, const void* b, int6
 int dk_argmax_finish(unsigned long long* keys, int64_t n_rows, int64_t* tokens, int64_t* tokens_copy,
                      int32_t* lens_a, int32_t* lens_b, void* stream);
 
+/* ---- Tensor-parallel decoder layers (no counterpart in the reference: its TinyModel runs on one
+ * device, kernels/tiny_model.py:99-140) ---- */
+/* Row-parallel layer output: the fold of dk_matmul_fold_slices (n_parts = 1, 2, 4 or 8 subtree sums in
+ * group order, partials[j * M * N + m * N + n]) followed by the epilogue `epi` exactly as
+ * dk_matmul_batch_invariant_ex applies it (DK_EPI_STORE, _RESIDUAL, _RESIDUAL_RMSNORM, _SILU, _SILU_MUL
+ * or _ARGMAX; NULL = DK_EPI_STORE), so a layer split over ranks returns the one-GPU fused bits. */
+int dk_matmul_fold_slices_ex(const float* partials, int n_parts, void* c, int64_t ldc, int64_t M, int64_t N,
+                             int dtype, const dk_matmul_epilogue* epi, void* stream);
+/* Greedy step end for a column-parallel LM head: keys[p * part_stride + r] (p < n_parts <= 8) are part
+ * p's DK_EPI_ARGMAX keys over its own columns, which start at column col_offsets[p] (host array) of the
+ * full vocabulary.  tokens[r] = the global argmax (largest value, then smallest column: the one-GPU
+ * answer); then as dk_argmax_finish, with reset_keys[r] = 0 for the caller's local key buffer (optional). */
+int dk_argmax_finish_parts(const unsigned long long* keys, int n_parts, int64_t part_stride,
+                           const int64_t* col_offsets, int64_t n_rows, int64_t* tokens, int64_t* tokens_copy,
+                           int32_t* lens_a, int32_t* lens_b, unsigned long long* reset_keys, void* stream);
+
 /* ---- Decode attention (one query per row, split-KV with a fixed split size) ----
  * q:   [n_rows, n_q_heads, head_dim], strides (q_stride_row, q_stride_head), unit d stride.
  * k,v: KV cache viewed as [kv_n_seq, n_kv_heads, kv_capacity, head_dim] with element strides
@@ -269,7 +285,9 @@ int dk_attention_batch_invariant_noalloc(const void* q, int64_t q_stride_row, in
  * [tokens, n_v_heads]; o: [tokens, n_v_heads, head_dim_v] in q's dtype, all contiguous, q/k/v
  * starting on a 16-byte boundary.  Value head j
  * uses query/key head j / (n_v_heads / n_heads).  Sequences: cu_seqlens (device int64[n_seqs + 1])
- * or, when NULL, n_seqs rows of seq_len tokens each.  initial_state / final_state: [n_seqs,
+ * with seq_len = the packed length T of q/k/v/g/beta/o (a sequence whose pair falls outside [0, T] or
+ * decreases is skipped and recorded as DK_ERR_DEVICE_CHECK, detail 0x500), or, when cu_seqlens is
+ * NULL, n_seqs rows of seq_len tokens each.  initial_state / final_state: [n_seqs,
  * n_v_heads, head_dim_k, head_dim_v] (final in f32), either may be NULL.  chunk_size 64 computes
  * 64-token chunks from each sequence's start (chunked form); 1 steps token by token in the order of
  * the recurrence (decode path; FLA's fused_recurrent_gated_delta_rule).  A sequence's

@@ -110,6 +110,25 @@ def silu(x):
     return x32 / (np.float32(1.0) + np.exp(-x32))
 
 
+class _SeqCache:
+    """One sequence's K or V cache of one layer: [Hkv, n, D] f32 in a buffer that doubles when full
+    (appending is O(1) amortised, where concatenating every step is O(n))."""
+
+    def __init__(self, hkv, d):
+        self.k = np.zeros((hkv, 16, d), dtype=np.float32)
+        self.v = np.zeros((hkv, 16, d), dtype=np.float32)
+        self.n = 0
+
+    def append(self, k, v):
+        if self.n == self.k.shape[1]:
+            grow = lambda a: np.concatenate([a, np.zeros_like(a)], axis=1)  # noqa: E731
+            self.k, self.v = grow(self.k), grow(self.v)
+        self.k[:, self.n] = k
+        self.v[:, self.n] = v
+        self.n += 1
+        return self.k[:, :self.n], self.v[:, :self.n]
+
+
 class TinyModelOracle:
     """Decode loop over numpy copies of a TinyModel's weights.
 
@@ -122,7 +141,7 @@ class TinyModelOracle:
         self.eps, self.mlp, self.dtype = eps, mlp, dtype
 
     def step(self, tokens, caches):
-        """tokens: [B] ints; caches: per layer list of per-sequence (k [Hkv, L, D], v) lists (mutated)."""
+        """tokens: [B] ints; caches: per layer list of per-sequence caches (``empty_caches``; mutated)."""
         dt = self.dtype
         H, Hkv, D = self.H, self.Hkv, self.D
         B = len(tokens)
@@ -134,10 +153,7 @@ class TinyModelOracle:
             v = matmul(xn, layer["w_v"], dt).reshape(B, Hkv, D)
             attn = np.zeros((B, H, D), dtype=np.float32)
             for b in range(B):
-                kc, vc = caches[li][b]
-                kc = np.concatenate([kc, k[b][:, None, :]], axis=1)
-                vc = np.concatenate([vc, v[b][:, None, :]], axis=1)
-                caches[li][b] = (kc, vc)
+                kc, vc = caches[li][b].append(k[b], v[b])
                 attn[b] = attention(q[b:b + 1], kc[None], vc[None], dtype=dt)[0]
             o = matmul(attn.reshape(B, H * D), layer["w_o"], dt)
             x = round_to(x + o, dt)
@@ -153,12 +169,15 @@ class TinyModelOracle:
         return matmul(xf, self.w["w_lm_head"], dt)
 
     def empty_caches(self, batch):
-        z = np.zeros((self.Hkv, 0, self.D), dtype=np.float32)
-        return [[(z, z) for _ in range(batch)] for _ in self.w["layers"]]
+        return [[_SeqCache(self.Hkv, self.D) for _ in range(batch)] for _ in self.w["layers"]]
 
-    def generate(self, prompts, n_steps):
-        """Greedy decode; prompts: list of token lists. Returns (tokens [B, n_steps], last logits)."""
+    def generate(self, prompts, n_steps, margins=None):
+        """Greedy decode; prompts: list of token lists. Returns (tokens [B, n_steps], last logits).
+        margins (optional list): receives per row the top-1 minus top-2 logit of every generated
+        token's step, so a caller can tell a near-tie from a real disagreement."""
         B = len(prompts)
+        if margins is not None:
+            margins[:] = [[] for _ in range(B)]
         caches = self.empty_caches(B)
         maxp = max(len(p) for p in prompts)
         # feed prompts token by token; a row whose prompt is exhausted starts generating
@@ -183,6 +202,9 @@ class TinyModelOracle:
                     nxt = int(np.argmax(logits[i]))
                     out[b].append(nxt)
                     cur[b] = nxt
+                    if margins is not None:
+                        top2 = np.partition(logits[i], -2)[-2:]
+                        margins[b].append(float(top2[1] - top2[0]))
         return np.asarray(out, dtype=np.int64), logits
 
 
@@ -197,10 +219,11 @@ class TinyModelOracle:
 # Value head j reads query/key head j // (HV / H).  State S is [K, V], f32.
 # --------------------------------------------------------------------------
 def gdn_recurrent(q, k, v, g, beta, scale=None, initial_state=None, cu_seqlens=None, dtype="bfloat16",
-                  acc=np.float32):
+                  acc=np.float32, v_heads=None):
     """q, k [T, H, K]; v [T, HV, V]; g, beta [T, HV]; initial_state [N, HV, K, V].
 
-    Returns (o [T, HV, V] rounded to dtype, final_state [N, HV, K, V] f32)."""
+    Returns (o [T, HV, V] rounded to dtype, final_state [N, HV, K, V] f32).  v_heads (optional):
+    compute only these value heads (the others stay zero) -- for long sequences."""
     q = np.asarray(q, dtype=acc)
     k = np.asarray(k, dtype=acc)
     v = np.asarray(v, dtype=acc)
@@ -218,7 +241,7 @@ def gdn_recurrent(q, k, v, g, beta, scale=None, initial_state=None, cu_seqlens=N
     final = np.zeros((N, HV, K, V), dtype=acc)
     for n in range(N):
         bos, eos = int(cu_seqlens[n]), int(cu_seqlens[n + 1])
-        for j in range(HV):
+        for j in (range(HV) if v_heads is None else v_heads):
             hq = j // grp
             S = np.zeros((K, V), dtype=acc) if initial_state is None else np.asarray(
                 initial_state[n, j], dtype=acc).copy()

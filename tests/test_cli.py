@@ -30,3 +30,24 @@ def test_kernel_bench_runs(dev):
         assert len(rep[section]) == 2
         for row in rep[section]:
             assert row["batch_invariant_ms"] > 0
+
+
+BENCH_MODEL_ARGS = ["--vocab-size", "32000", "--num-layers", "4", "--num-heads", "16", "--head-dim", "64",
+                    "--mlp-hidden", "2816", "--mlp", "swiglu", "--dtype", "bfloat16", "--prompt-len", "32",
+                    "--other-len", "16,512", "--steps", "128"]
+
+
+def test_kernel_check_benchmark_model_10_runs(dev):
+    """The benchmark model: the tracked 32-token prompt among freshly drawn co-batches of 16-512
+    token prompts, 128 greedy tokens, 10 runs at each batch size 1, 8, 64, 256."""
+    from detkernels_b200.kernels.integration import main
+    rep = main(BENCH_MODEL_ARGS + ["--batch-sizes", "1,8,64,256", "--runs", "10"])
+    assert all(r["all_identical"] and r["n_diverging"] == 0 for r in rep["batch_size_results"]), rep
+    assert rep["across_batch_sizes_and_tp"]["all_identical"], rep
+
+
+def test_kernel_check_benchmark_model_across_tp(dev):
+    """The same tracked tokens at TP 1, 2, 4, 8 (ranks held in this process) and batch 8 / 64."""
+    from detkernels_b200.kernels.integration import main
+    rep = main(BENCH_MODEL_ARGS + ["--batch-sizes", "8,64", "--runs", "3", "--tp", "1,2,4,8"])
+    assert rep["across_batch_sizes_and_tp"]["all_identical"], rep

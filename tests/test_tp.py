@@ -7,6 +7,7 @@ import socket
 import numpy as np
 import pytest
 
+from _ranks import collect
 from oracle import ops as oracle
 from oracle.numerics import round_to
 
@@ -71,7 +72,7 @@ def test_row_and_column_parallel_bookkeeping_on_cpu_ranks(world, K):
     procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, K, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=120) for _ in range(world)]
+    results = collect(q, procs, world, 120)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -154,7 +155,7 @@ def test_nccl_row_parallel_matches_one_gpu():
     procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=300) for _ in range(world)]
+    res = collect(q, procs, world, 300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
