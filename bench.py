@@ -701,12 +701,31 @@ def main(argv=None):
     ap.add_argument("--skip-gdn", action="store_true", help="skip the gated-delta-rule section")
     ap.add_argument("--gdn-only", action="store_true", help="run and print only the gated-delta-rule section")
     ap.add_argument("--rmsnorm-only", action="store_true", help="run and print only the RMSNorm roofline section")
+    ap.add_argument("--gemm-only", default=None, metavar="M,N",
+                    help="run and print only matmul_batch_invariant [M,4096] x [4096,N] against cuBLAS (profiling)")
+    ap.add_argument("--gemm-kernel", choices=["auto", "one", "pair"], default="auto",
+                    help="with --gemm-only: the planner's kernel, the one-CTA kernel or the CTA-pair kernel")
     ap.add_argument("--tp", type=int, default=1, choices=[1, 2, 4, 8],
                     help="tensor-parallel decode over the torchrun ranks (needs --nproc-per-node TP)")
     ap.add_argument("--new-tokens", type=int, default=NEW_TOKENS,
                     help="tokens generated per prompt (the workload is 128; smaller only for profiling)")
     args = ap.parse_args(argv)
     NEW_TOKENS = args.new_tokens
+    if args.gemm_only:
+        import torch
+        torch.cuda.set_device(0)
+        m, n = (int(v) for v in args.gemm_only.split(","))
+        if args.gemm_kernel != "auto":
+            import ctypes
+
+            from detkernels_b200 import _lib
+            hook = _lib.load().dk_matmul_pair_schedule_for_test   # not in the public header
+            hook.restype, hook.argtypes = ctypes.c_int, [ctypes.c_int]
+            hook(1 if args.gemm_kernel == "one" else 2)
+        global GEMM_SHAPES
+        GEMM_SHAPES = [(m, n)]
+        print(json.dumps({"gemm_vs_cublas": gemm_vs_cublas(iters=5)}), flush=True)
+        return 0
     if args.gdn_only or args.rmsnorm_only:
         import torch
         torch.cuda.set_device(0)

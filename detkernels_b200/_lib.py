@@ -76,6 +76,10 @@ SIGNATURES = {
     "dk_attention_batch_invariant": (_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64,
                                             _i64, _c_void_p, _i64, _i64, _c_void_p, _i32, _c_void_p, _i32, _i32,
                                             _i32, _i32, _i32, _i32, _f32, _int, _c_void_p, _size, _c_void_p]),
+    "dk_attention_paged_batch_invariant": (_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64,
+                                                  _i64, _i32, _c_void_p, _i64, _i64, _i32, _c_void_p, _i64, _i64,
+                                                  _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _i32, _i32, _i32,
+                                                  _f32, _int, _c_void_p, _size, _c_void_p]),
     "dk_attention_noalloc_scratch_limit": (_size, []),
     "dk_attention_batch_invariant_noalloc": (_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64,
                                                     _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i32, _c_void_p,
@@ -88,7 +92,7 @@ SIGNATURES = {
 
 
 # layout version of the structs mirrored here (DK_ABI_VERSION of include/detkernels_b200.h)
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 DK_EPI_STORE = 0
 DK_EPI_RESIDUAL = 1
@@ -107,7 +111,9 @@ class MatmulEpilogue(ctypes.Structure):
                 ("cache_stride_seq", ctypes.c_int64), ("cache_stride_head", ctypes.c_int64),
                 ("cache_stride_tok", ctypes.c_int64), ("row_seq", ctypes.c_void_p), ("row_pos", ctypes.c_void_p),
                 ("argmax_keys", ctypes.c_void_p), ("norm_w", ctypes.c_void_p), ("norm_w_dtype", ctypes.c_int),
-                ("norm_out", ctypes.c_void_p), ("norm_ld", ctypes.c_int64), ("norm_eps", ctypes.c_float)]
+                ("norm_out", ctypes.c_void_p), ("norm_ld", ctypes.c_int64), ("norm_eps", ctypes.c_float),
+                ("block_table", ctypes.c_void_p), ("block_table_stride", ctypes.c_int64),
+                ("page_size", ctypes.c_int32), ("blocks_per_seq", ctypes.c_int32), ("n_blocks", ctypes.c_int64)]
 
 
 class DetKernelsError(RuntimeError):

@@ -89,6 +89,12 @@ struct Params {
   int32_t upt;        // CTAs per (tile, kv head) = ceil(max_splits / spu)
   int32_t kv_capacity;
   int32_t kv_n_seq;
+  // paged KV (block_table != null): the tensor maps cover a block pool [n_blocks, hkv, page, d];
+  // token t of sequence s lives in block block_table[s * bt_stride + t / page] at t % page
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int32_t page;       // tokens per block, a multiple of kBlock
+  int32_t n_blocks;
   float scale_log2;   // softmax scale * log2(e)
   float* ws_o;        // [n_tiles][hkv][max_splits][rows_cap][D]
   float* ws_ml;       // [n_tiles][hkv][max_splits][rows_cap][2]
@@ -103,7 +109,27 @@ enum : int {
   kDetItem = 0x204,
   kDetLen = 0x210,   // a kv_len exceeds the cache capacity or max_kv_len
   kDetTile = 0x211,  // a row tile is malformed
+  kDetPage = 0x212,  // a block table entry outside the block pool
 };
+
+// TMA coordinates (token, slab) of the 64-token block starting at token t0 of sequence seq:
+// (t0, seq) for a contiguous cache; (t0 mod page, block) through the block table for a paged
+// one.  A table entry outside the pool is recorded (DK_ERR_DEVICE_CHECK) and replaced by block 0,
+// so the copy always stays inside the pool.
+__device__ __forceinline__ void kv_block_coords(const Params& p, int seq, int t0, int& tok, int& slab) {
+  if (p.block_table == nullptr) {
+    tok = t0;
+    slab = seq;
+    return;
+  }
+  const int pg = t0 / p.page;
+  tok = t0 - pg * p.page;
+  slab = p.block_table[static_cast<int64_t>(seq) * p.bt_stride + pg];
+  if (slab < 0 || slab >= p.n_blocks) {
+    report_error(DK_ERR_DEVICE_CHECK, kDetPage);
+    slab = 0;
+  }
+}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -346,11 +372,13 @@ __global__ void __launch_bounds__(kThreads, (D == 128 || (!T1 && KM >= 8)) ? 2 :
             uint8_t* st = ring + stage * C::STAGE_BYTES;
             mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
             const int t0 = tb + b * kBlock;
+            int tok, slab;
+            kv_block_coords(p, it.seq, t0, tok, slab);
 #pragma unroll
             for (int bx = 0; bx < C::NBOX; ++bx) {
-              tma_load_4d(st + bx * C::BOX_BYTES, &tmK, &full[stage], bx * C::BOXD, t0, it.kvh, it.seq);
-              tma_load_4d(st + C::TENSOR_BYTES + bx * C::BOX_BYTES, &tmV, &full[stage], bx * C::BOXD, t0, it.kvh,
-                          it.seq);
+              tma_load_4d(st + bx * C::BOX_BYTES, &tmK, &full[stage], bx * C::BOXD, tok, it.kvh, slab);
+              tma_load_4d(st + C::TENSOR_BYTES + bx * C::BOX_BYTES, &tmV, &full[stage], bx * C::BOXD, tok, it.kvh,
+                          slab);
             }
             ++fills;
             if (++stage == C::STAGES) {

@@ -117,6 +117,7 @@ struct Params {
   int group;                     // slices per work unit (aligned group, power of two)
   int n_tiles, m_tiles;
   int mode;
+  int pair;        // 1: CTA-pair kernel (n_tiles counts 256-column pair tiles)
   int a_rows;      // rows of the activation TMA box (128, or fewer when M fits one tile)
   void* c;
   int64_t ldc;
@@ -169,6 +170,33 @@ __device__ __forceinline__ float rnd(float v) {
   return to_f32<T>(from_f32<T>(v));
 }
 
+// Element offset of (row m's sequence, head, row m's position, d) in a K/V cache: contiguous
+// [n_seq, heads, capacity, d], or paged through the block table (block = table[seq][pos / page],
+// token pos % page of a [n_blocks, heads, page, d] pool).  A position beyond the table row or a
+// table entry outside the pool is recorded (DK_ERR_DEVICE_CHECK) and the store skipped (ok = false).
+__device__ __forceinline__ int64_t kv_cache_offset(const dk_matmul_epilogue& e, int m, int head, int d, bool& ok) {
+  const int64_t seq = e.row_seq ? e.row_seq[m] : m;
+  int64_t pos = e.row_pos[m];
+  int64_t slab = seq;
+  ok = true;
+  if (e.block_table) {
+    const int64_t pg = pos / e.page_size;
+    if (pos < 0 || pg >= e.blocks_per_seq) {
+      report_error(DK_ERR_DEVICE_CHECK, 0x600);
+      ok = false;
+      return 0;
+    }
+    slab = e.block_table[seq * e.block_table_stride + pg];
+    if (slab < 0 || slab >= e.n_blocks) {
+      report_error(DK_ERR_DEVICE_CHECK, 0x601);
+      ok = false;
+      return 0;
+    }
+    pos -= pg * e.page_size;
+  }
+  return slab * e.cache_stride_seq + head * e.cache_stride_head + pos * e.cache_stride_tok + d;
+}
+
 // Final value v of output element (m, n) -> memory, per the epilogue mode (all but SILU_MUL).
 template <typename T>
 __device__ __forceinline__ void store_final(const Params& p, T* C, int m, int n, float v) {
@@ -190,10 +218,10 @@ __device__ __forceinline__ void store_final(const Params& p, T* C, int m, int n,
         const int which = j / e.kv_cols;
         const int jj = j - which * e.kv_cols;
         const int head = jj / e.head_dim, d = jj - head * e.head_dim;
-        const int64_t seq = e.row_seq ? e.row_seq[m] : m;
         T* cache = static_cast<T*>(which == 0 ? e.k_cache : e.v_cache);
-        cache[seq * e.cache_stride_seq + head * e.cache_stride_head +
-              static_cast<int64_t>(e.row_pos[m]) * e.cache_stride_tok + d] = from_f32<T>(v);
+        bool ok;
+        const int64_t off = kv_cache_offset(e, m, head, d, ok);
+        if (ok) cache[off] = from_f32<T>(v);
       }
       break;
     }
@@ -345,10 +373,10 @@ __device__ __forceinline__ void store_final_row(const Params& p, T* C, int m, in
         const int which = j / e.kv_cols;
         const int jj = j - which * e.kv_cols;
         const int head = jj / e.head_dim, d0 = jj - head * e.head_dim;
-        const int64_t seq = e.row_seq ? e.row_seq[m] : m;
         T* cache = static_cast<T*>(which == 0 ? e.k_cache : e.v_cache);
-        const int64_t off = seq * e.cache_stride_seq + head * e.cache_stride_head +
-                            static_cast<int64_t>(e.row_pos[m]) * e.cache_stride_tok + d0;
+        bool ok;
+        const int64_t off = kv_cache_offset(e, m, head, d0, ok);
+        if (!ok) return;
         if (reinterpret_cast<uintptr_t>(cache + off) % 16 == 0) {
           store_row_vec<T>(cache + off, v, 32);
         } else {
@@ -887,10 +915,13 @@ __global__ void argmax_finish_parts_kernel(const unsigned long long* __restrict_
   for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < n_rows;
        r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     unsigned long long best = 0ull;
-    for (int q = 0; q < n_parts; ++q) {
-      unsigned long long k = keys[q * part_stride + r];
-      if (k != 0ull) k -= static_cast<unsigned long long>(offs.v[q]);
-      best = k > best ? k : best;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (q < n_parts) {
+        unsigned long long k = keys[q * part_stride + r];
+        if (k != 0ull) k -= static_cast<unsigned long long>(offs.v[q]);
+        best = k > best ? k : best;
+      }
     }
     const int64_t col = static_cast<int64_t>(~static_cast<uint32_t>(best & 0xffffffffull));
     tokens[r] = col;

@@ -15,6 +15,7 @@
 #include "dk_common.cuh"
 #include "dk_rmsnorm.cuh"
 #include "dk_gemm.cuh"
+#include "dk_gemm2.cuh"
 #include "dk_attention.cuh"
 #include "dk_attention_variant.cuh"
 #include "dk_gdn.cuh"
@@ -140,14 +141,40 @@ int encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* b
 bool valid_dtype(int d) { return d == DK_F32 || d == DK_F16 || d == DK_BF16; }
 
 // ============================ RMSNorm ============================
+// Persistent vector RMSNorm over `rows` rows of at most MAXC * 256 chunks: as many CTAs as fit
+// on the GPU at once (never more than rows), each walking rows b, b + grid, ...
+template <typename T, typename W, int MAXC>
+cudaError_t rmsnorm_persistent(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows,
+                               int64_t cols, float eps, cudaStream_t st) {
+  static int per_sm[kMaxDevices] = {};
+  const int dev = current_device();
+  auto fn = dk::rmsnorm_inv_vec_persistent_kernel<T, W, MAXC>;
+  int blocks = (dev >= 0 && dev < kMaxDevices) ? per_sm[dev] : 0;
+  if (blocks <= 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, dk::kRmsThreads, 0) != cudaSuccess || blocks <= 0)
+      blocks = 1;
+    if (dev >= 0 && dev < kMaxDevices) per_sm[dev] = blocks;
+  }
+  const int64_t cap = static_cast<int64_t>(blocks) * sm_count(dev);
+  const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
+  return launch_pdl(fn, dim3(grid), dim3(dk::kRmsThreads), 0, st, static_cast<const T*>(x), xs,
+                    static_cast<const W*>(w), static_cast<T*>(y), ys, rows, cols, eps);
+}
+
 template <typename T, typename W>
 int rmsnorm_inv_launch(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int64_t cols,
                        float eps, cudaStream_t st) {
   constexpr int VEC = dk::Vec16<T>::N;
   const bool vec = (cols % VEC == 0) && (xs % VEC == 0) && (ys % VEC == 0) && aligned16(x) && aligned16(y);
   const dim3 grid(static_cast<unsigned>(rows));
+  const int64_t per_thread = (cols / VEC + dk::kRmsThreads - 1) / dk::kRmsThreads;   // chunks per thread
   cudaError_t e;
-  if (vec) {
+  if (vec && rows > 1 && per_thread >= 3 && per_thread <= 4) {
+    // rows of 3-4 chunks per thread (12-16 KB: 4096 f32, 8192 16-bit elements): persistent, each
+    // CTA holding its next row in flight.  Shorter rows keep one CTA per row (measured: a
+    // persistent CTA's per-row barriers then dominate).
+    e = rmsnorm_persistent<T, W, 4>(x, xs, w, y, ys, rows, cols, eps, st);
+  } else if (vec) {
     constexpr int MAXC = (sizeof(T) == 4) ? 8 : 4;
     e = launch_pdl(dk::rmsnorm_inv_vec_kernel<T, W, MAXC>, grid, dim3(dk::kRmsThreads), 0, st,
                    static_cast<const T*>(x), xs, static_cast<const W*>(w), static_cast<T*>(y), ys, cols, eps);
@@ -233,6 +260,7 @@ int slice_len_for(int64_t K, int n_slices) {
 struct GemmPlan {
   int mode;
   int group;
+  bool pair;           // CTA-pair kernel (n_tiles then counts 256-column pair tiles)
   int n_tiles, m_tiles;
   size_t ws_bytes;     // workspace bytes this plan needs
   size_t counters_off; // byte offset of the counters region
@@ -269,11 +297,26 @@ int pick_group(int64_t M, int64_t N, int64_t K, int64_t tiles, int sms) {
   return best_g;
 }
 
+// Which GEMM kernel runs an invariant call (never changes the arithmetic): 0 = the planner's
+// choice, 1 = always the one-CTA kernel, 2 = always the CTA-pair kernel.  Only the test hook
+// dk_matmul_pair_schedule_for_test sets it.
+int g_pair_override = 0;
+
+// The CTA-pair kernel moves 24 KB per SM per 128 x 128 x 64 of work instead of 32 KB, but
+// measured on B200 it is not yet faster than the one-CTA kernel (M = 2048, N = 4096: 147 vs
+// 129 us), so the planner keeps the one-CTA kernel; the pair kernel runs when forced.
+bool use_pair_kernel(int64_t M, int64_t N) {
+  (void)M;
+  (void)N;
+  return g_pair_override == 2;
+}
+
 GemmPlan plan_invariant(int64_t M, int64_t N, int64_t K, int sms) {
   GemmPlan pl{};
-  pl.n_tiles = static_cast<int>(ceil_div(N, dk::gemm::kTileN));
+  pl.pair = use_pair_kernel(M, N);
+  pl.n_tiles = static_cast<int>(ceil_div(N, pl.pair ? dk::gemm::kPairTileN : dk::gemm::kTileN));
   pl.m_tiles = static_cast<int>(ceil_div(M, dk::gemm::kTileM));
-  const int64_t tiles = static_cast<int64_t>(pl.n_tiles) * pl.m_tiles;
+  const int64_t tiles = static_cast<int64_t>(pl.n_tiles) * pl.m_tiles * (pl.pair ? 2 : 1);   // in CTAs
   const int group = pick_group(M, N, K, tiles, sms);
   pl.group = group;
   pl.mode = (group == dk::gemm::kSlices) ? dk::gemm::FOLD : dk::gemm::SPLIT;
@@ -355,9 +398,44 @@ int launch_fold_norm(int dtype, const float* partials, int n_parts, const dk::ge
   return dk_rmsnorm_batch_invariant(p.c, p.ldc, nm.w, nm.out, nm.ld, p.M, p.N, dtype, nm.w_dtype, nm.eps, st);
 }
 
+// The CTA-pair kernel's launch: clusters of 2, as many pairs as can be resident at once.
+template <typename T, int FMT, bool FOLDK>
+cudaError_t launch_pair(const CUtensorMap& tmB, const CUtensorMap& tmA, const dk::gemm::Params& p, int64_t units,
+                        cudaStream_t st, int* rc) {
+  auto fn = dk::gemm::gemm_pair_kernel<T, FMT, FOLDK>;
+  static bool done[kMaxDevices] = {};
+  static int max_pairs[kMaxDevices] = {};
+  *rc = ensure_smem(fn, dk::gemm::kSmemBytes, done);
+  if (*rc) return cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(dk::gemm::kThreads);
+  cfg.dynamicSmemBytes = dk::gemm::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const int dev = current_device();
+  int pairs = (dev >= 0 && dev < kMaxDevices) ? max_pairs[dev] : 0;
+  if (pairs <= 0) {
+    cfg.gridDim = dim3(2 * 64);
+    if (cudaOccupancyMaxActiveClusters(&pairs, fn, &cfg) != cudaSuccess || pairs <= 0) pairs = sm_count(dev) / 2;
+    if (dev >= 0 && dev < kMaxDevices) max_pairs[dev] = pairs;
+  }
+  const int64_t n = units < pairs ? units : pairs;
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * n));
+  return cudaLaunchKernelEx(&cfg, fn, tmB, tmA, p);
+}
+
 int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb, dk::gemm::Params p,
                 cudaStream_t st, const char* what, const NormSpec* norm = nullptr) {
-  p.a_rows = (p.m_tiles == 1) ? static_cast<int>(ceil_div(p.M, 8) * 8) : dk::gemm::kTileM;
+  p.a_rows = p.pair ? dk::gemm::kPairRows
+                    : ((p.m_tiles == 1) ? static_cast<int>(ceil_div(p.M, 8) * 8) : dk::gemm::kTileM);
   const int64_t k_mem = p.k_extent > 0 ? p.k_extent : p.K;
   CUtensorMap tmB, tmA;
   const uint64_t dimsB[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(k_mem)};
@@ -379,7 +457,16 @@ int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ld
   if (grid <= 0) return DK_OK;
   cudaError_t e;
   const bool fold = (p.mode == dk::gemm::FOLD);
-  if (dtype == DK_BF16) {
+  if (p.pair) {
+    int lrc = DK_OK;
+    if (dtype == DK_BF16)
+      e = fold ? launch_pair<__nv_bfloat16, 1, true>(tmB, tmA, p, units, st, &lrc)
+               : launch_pair<__nv_bfloat16, 1, false>(tmB, tmA, p, units, st, &lrc);
+    else
+      e = fold ? launch_pair<__half, 0, true>(tmB, tmA, p, units, st, &lrc)
+               : launch_pair<__half, 0, false>(tmB, tmA, p, units, st, &lrc);
+    if (lrc) return lrc;
+  } else if (dtype == DK_BF16) {
     static bool done[2][kMaxDevices] = {};
     auto fn = fold ? dk::gemm::gemm_kernel<__nv_bfloat16, 1, true> : dk::gemm::gemm_kernel<__nv_bfloat16, 1, false>;
     if ((rc = ensure_smem(fn, dk::gemm::kSmemBytes, done[fold]))) return rc;
@@ -737,6 +824,9 @@ int dk_matmul_batch_invariant_ex(const void* a, int64_t lda, const void* b, int6
       if (e.q_cols < 0 || e.kv_cols <= 0 || e.head_dim <= 0 || e.kv_cols % e.head_dim ||
           static_cast<int64_t>(e.q_cols) + 2LL * e.kv_cols != N || !e.k_cache || !e.v_cache || !e.row_pos)
         return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad QKV cache epilogue", what);
+      if (e.block_table && (e.page_size <= 0 || e.blocks_per_seq <= 0 || e.n_blocks <= 0 ||
+                            e.block_table_stride < e.blocks_per_seq))
+        return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad paged KV fields (page_size, blocks_per_seq, n_blocks)", what);
       out_cols = e.q_cols;
       break;
     default:
@@ -762,6 +852,7 @@ int dk_matmul_batch_invariant_ex(const void* a, int64_t lda, const void* b, int6
   p.n_tiles = pl.n_tiles;
   p.m_tiles = pl.m_tiles;
   p.mode = pl.mode;
+  p.pair = pl.pair ? 1 : 0;
   p.c = c;
   p.ldc = ldc;
   if (pl.mode == dk::gemm::SPLIT) {
@@ -1014,14 +1105,30 @@ size_t dk_attention_workspace_size(int32_t n_tiles, int32_t rows_per_tile, int32
   return plan_attention(n_tiles, rows_per_tile, n_q_heads, n_kv_heads, head_dim, max_kv_len).total;
 }
 
-int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_stride_head, const void* k,
-                                 const void* v, int64_t kv_stride_seq, int64_t kv_stride_head, int64_t kv_stride_tok,
-                                 int64_t kv_n_seq, int64_t kv_capacity, void* out, int64_t out_stride_row,
-                                 int64_t out_stride_head, const int32_t* kv_lens, int32_t uniform_kv_len,
-                                 const int32_t* row_tiles, int32_t n_tiles, int32_t n_rows, int32_t n_q_heads,
-                                 int32_t n_kv_heads, int32_t head_dim, int32_t max_kv_len, float scale, int dtype,
-                                 void* workspace, size_t workspace_bytes, void* stream) {
-  const char* what = "attention_batch_invariant";
+}  // extern "C"
+
+namespace {
+
+// Paged KV description (null: a contiguous [n_seq, heads, capacity, d] cache).
+struct PagedKV {
+  const int32_t* table;
+  int64_t table_stride;
+  int32_t page;
+  int32_t blocks_per_seq;
+  int64_t n_blocks;
+};
+
+// The invariant decode attention over a contiguous cache (pg == nullptr; kv_stride_seq /
+// kv_n_seq / kv_capacity describe it) or a paged one (the strides describe the block pool;
+// kv_n_seq is the number of block-table rows and the capacity blocks_per_seq * page).
+int attention_invariant_impl(const void* q, int64_t q_stride_row, int64_t q_stride_head, const void* k,
+                             const void* v, int64_t kv_stride_seq, int64_t kv_stride_head, int64_t kv_stride_tok,
+                             int64_t kv_n_seq, int64_t kv_capacity, void* out, int64_t out_stride_row,
+                             int64_t out_stride_head, const int32_t* kv_lens, int32_t uniform_kv_len,
+                             const int32_t* row_tiles, int32_t n_tiles, int32_t n_rows, int32_t n_q_heads,
+                             int32_t n_kv_heads, int32_t head_dim, int32_t max_kv_len, float scale, int dtype,
+                             void* workspace, size_t workspace_bytes, void* stream, const PagedKV* pg,
+                             const char* what) {
   if (dtype != DK_BF16 && dtype != DK_F16) return fail(DK_ERR_UNSUPPORTED, "%s: dtype must be bf16 or f16", what);
   if (head_dim != 32 && head_dim != 64 && head_dim != 128)
     return fail(DK_ERR_UNSUPPORTED, "%s: head_dim %d not in {32, 64, 128}", what, head_dim);
@@ -1032,6 +1139,14 @@ int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_
   if (n_kv_heads > 65535) return fail(DK_ERR_INVALID_ARGUMENT, "%s: too many kv heads", what);
   if (n_rows == 0) return DK_OK;
   if (!q || !k || !v || !out) return fail(DK_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  if (pg) {
+    if (!pg->table || pg->page <= 0 || pg->page % dk::attn::kBlock || pg->blocks_per_seq <= 0 ||
+        pg->n_blocks <= 0 || pg->n_blocks > 0x7fffffffLL || pg->table_stride < pg->blocks_per_seq)
+      return fail(DK_ERR_INVALID_ARGUMENT,
+                  "%s: paged KV needs a block table, page_size a multiple of %d, blocks_per_seq > 0, "
+                  "n_blocks > 0 and block_table_stride >= blocks_per_seq", what, dk::attn::kBlock);
+    kv_capacity = static_cast<int64_t>(pg->page) * pg->blocks_per_seq;
+  }
   if (max_kv_len < 0 || kv_capacity <= 0 || kv_n_seq <= 0 || kv_capacity > 0x7fffffffLL || kv_n_seq > 0x7fffffffLL)
     return fail(DK_ERR_INVALID_ARGUMENT, "%s: bad KV extents", what);
   if (!kv_lens && (uniform_kv_len < 0 || uniform_kv_len > max_kv_len || uniform_kv_len > kv_capacity))
@@ -1076,6 +1191,12 @@ int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_
   p.upt = pl.upt;
   p.kv_capacity = static_cast<int32_t>(kv_capacity);
   p.kv_n_seq = static_cast<int32_t>(kv_n_seq);
+  if (pg) {
+    p.block_table = pg->table;
+    p.bt_stride = pg->table_stride;
+    p.page = pg->page;
+    p.n_blocks = static_cast<int32_t>(pg->n_blocks);
+  }
   p.scale_log2 = scale * 1.4426950408889634f;
   if (pl.total > 0) {
     if (static_cast<int64_t>(n_tiles) * n_kv_heads > kMaxCounters)
@@ -1087,11 +1208,11 @@ int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_
     p.counters = static_cast<int32_t*>(workspace);
   }
 
-  // K/V tensor maps: 4-D (d, token, kv head, sequence)
+  // K/V tensor maps: 4-D (d, token, kv head, sequence) -- or (d, token in block, kv head, block)
   CUtensorMap tk, tv;
   const int boxd = head_dim < 64 ? head_dim : 64;
-  const uint64_t dims[4] = {static_cast<uint64_t>(head_dim), static_cast<uint64_t>(kv_capacity),
-                            static_cast<uint64_t>(n_kv_heads), static_cast<uint64_t>(kv_n_seq)};
+  const uint64_t dims[4] = {static_cast<uint64_t>(head_dim), static_cast<uint64_t>(pg ? pg->page : kv_capacity),
+                            static_cast<uint64_t>(n_kv_heads), static_cast<uint64_t>(pg ? pg->n_blocks : kv_n_seq)};
   const uint64_t strides[3] = {static_cast<uint64_t>(kv_stride_tok) * 2, static_cast<uint64_t>(kv_stride_head) * 2,
                                static_cast<uint64_t>(kv_stride_seq) * 2};
   const uint32_t box[4] = {static_cast<uint32_t>(boxd), static_cast<uint32_t>(dk::attn::kBlock), 1, 1};
@@ -1112,6 +1233,42 @@ int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_
   if (head_dim == 32) return attn_launch<__half, 32>(tk, tv, p, n_items, st);
   if (head_dim == 64) return attn_launch<__half, 64>(tk, tv, p, n_items, st);
   return attn_launch<__half, 128>(tk, tv, p, n_items, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_stride_head, const void* k,
+                                 const void* v, int64_t kv_stride_seq, int64_t kv_stride_head, int64_t kv_stride_tok,
+                                 int64_t kv_n_seq, int64_t kv_capacity, void* out, int64_t out_stride_row,
+                                 int64_t out_stride_head, const int32_t* kv_lens, int32_t uniform_kv_len,
+                                 const int32_t* row_tiles, int32_t n_tiles, int32_t n_rows, int32_t n_q_heads,
+                                 int32_t n_kv_heads, int32_t head_dim, int32_t max_kv_len, float scale, int dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  return attention_invariant_impl(q, q_stride_row, q_stride_head, k, v, kv_stride_seq, kv_stride_head,
+                                  kv_stride_tok, kv_n_seq, kv_capacity, out, out_stride_row, out_stride_head,
+                                  kv_lens, uniform_kv_len, row_tiles, n_tiles, n_rows, n_q_heads, n_kv_heads,
+                                  head_dim, max_kv_len, scale, dtype, workspace, workspace_bytes, stream, nullptr,
+                                  "attention_batch_invariant");
+}
+
+int dk_attention_paged_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_stride_head,
+                                       const void* k_pool, const void* v_pool, int64_t pool_stride_block,
+                                       int64_t pool_stride_head, int64_t pool_stride_tok, int64_t n_blocks,
+                                       int32_t page_size, const int32_t* block_table, int64_t block_table_stride,
+                                       int64_t kv_n_seq, int32_t blocks_per_seq, void* out, int64_t out_stride_row,
+                                       int64_t out_stride_head, const int32_t* kv_lens, int32_t uniform_kv_len,
+                                       const int32_t* row_tiles, int32_t n_tiles, int32_t n_rows,
+                                       int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_kv_len,
+                                       float scale, int dtype, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  const PagedKV pg{block_table, block_table_stride, page_size, blocks_per_seq, n_blocks};
+  return attention_invariant_impl(q, q_stride_row, q_stride_head, k_pool, v_pool, pool_stride_block,
+                                  pool_stride_head, pool_stride_tok, kv_n_seq, 0, out, out_stride_row,
+                                  out_stride_head, kv_lens, uniform_kv_len, row_tiles, n_tiles, n_rows, n_q_heads,
+                                  n_kv_heads, head_dim, max_kv_len, scale, dtype, workspace, workspace_bytes, stream,
+                                  &pg, "attention_paged_batch_invariant");
 }
 
 size_t dk_attention_variant_workspace_size(int32_t batch, int32_t n_heads, int32_t head_dim) {
@@ -1185,6 +1342,15 @@ int dk_attention_batch_variant(const void* q, int64_t q_stride_b, int64_t q_stri
 // device address is looked up once per device with cudaGetSymbolAddress and cached.
 // ---------------------------------------------------------------------------------------------
 size_t dk_attention_noalloc_scratch_limit(void) { return kNoAllocScratchBytes; }
+
+// Test hook, deliberately absent from the public header: which kernel runs invariant matmuls
+// (0 = the planner's choice, 1 = one-CTA kernel, 2 = CTA-pair kernel), so a test can compare the
+// two schedules' bits on the same shapes.  Returns the previous setting.
+int dk_matmul_pair_schedule_for_test(int mode) {
+  const int prev = g_pair_override;
+  if (mode >= 0 && mode <= 2) g_pair_override = mode;
+  return prev;
+}
 
 // Test hook, deliberately absent from the public header: writes `value` into the first `bytes`
 // bytes of the no-alloc scratch on the current device (synchronously), so a test can show that

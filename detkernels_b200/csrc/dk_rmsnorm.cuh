@@ -112,6 +112,74 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_inv_vec_kernel(const T* _
   }
 }
 
+// Persistent form of rmsnorm_inv_vec_kernel for rows of at most MAXC * 256 chunks: CTA b
+// normalises rows b, b + gridDim.x, ... and issues the loads of its next row before it
+// reduces the current one, so every CTA keeps a row's worth of loads in flight.  Per row the
+// arithmetic is the vector kernel's (thread t owns chunks t, t + 256, ...; same FMA order,
+// same butterflies), so the bits do not depend on which CTA takes a row.
+template <typename T, typename W, int MAXC>
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_inv_vec_persistent_kernel(const T* __restrict__ x, int64_t xs,
+                                                                                  const W* __restrict__ w,
+                                                                                  T* __restrict__ y, int64_t ys,
+                                                                                  int64_t n_rows, int64_t n_cols,
+                                                                                  float eps) {
+  pdl_wait();   // x may come from the previous kernel
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  constexpr int VEC = Vec16<T>::N;
+  __shared__ float red[9];
+  const int64_t nchunks = n_cols / VEC;
+  int64_t row = blockIdx.x;
+  if (row >= n_rows) return;
+  Vec16<T> cur[MAXC];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int64_t c = threadIdx.x + (int64_t)i * kRmsThreads;
+    if (c < nchunks) cur[i] = *reinterpret_cast<const Vec16<T>*>(x + row * xs + c * VEC);
+  }
+  for (; row < n_rows; row += gridDim.x) {
+    const int64_t nrow = row + gridDim.x;
+    Vec16<T> nxt[MAXC];
+    if (nrow < n_rows) {
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int64_t c = threadIdx.x + (int64_t)i * kRmsThreads;
+        if (c < nchunks) nxt[i] = *reinterpret_cast<const Vec16<T>*>(x + nrow * xs + c * VEC);
+      }
+    }
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int64_t c = threadIdx.x + (int64_t)i * kRmsThreads;
+      if (c < nchunks) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float f = to_f32<T>(cur[i].v[j]);
+          acc = __fmaf_rn(f, f, acc);
+        }
+      }
+    }
+    const float total = block_sum_256(acc, red);
+    const float var = __fdiv_rn(total, (float)n_cols);
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    T* yr = y + row * ys;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int64_t c = threadIdx.x + (int64_t)i * kRmsThreads;
+      if (c < nchunks) {
+        Vec16<T> o;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float xn = __fmul_rn(to_f32<T>(cur[i].v[j]), rstd);
+          o.v[j] = from_f32<T>(__fmul_rn(xn, to_f32<W>(w[c * VEC + j])));
+        }
+        *reinterpret_cast<Vec16<T>*>(yr + c * VEC) = o;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) cur[i] = nxt[i];
+  }
+}
+
 // Embedding lookup fused into the invariant RMSNorm: row r reads table row idx[r], copies it
 // to x_out (the residual stream) and normalises it with exactly rmsnorm_inv_vec_kernel's
 // arithmetic.  An index outside [0, table_rows) records DK_ERR_DEVICE_CHECK and leaves the

@@ -64,19 +64,27 @@ def attention_reference(q, k, v, scale: float | None = None, *, kv_lens=None):
 
 
 def attention_decode(q, k_cache, v_cache, kv_lens, *, scale=None, row_tiles=None, max_kv_len=None, out=None,
-                     workspace=None):
+                     workspace=None, block_table=None):
     """General entry: q [R, H, D] rows over a KV cache [N_seq, H_kv, capacity, D].
 
     kv_lens: int32 CUDA tensor [R] (or an int for every row).  row_tiles:
     optional int32 CUDA tensor [T, 3] (first row, row count, sequence) grouping
     consecutive rows of one sequence; without it row r reads sequence r.
     max_kv_len: host-side bound on every kv_len (defaults to the capacity).
+    block_table: optional int32 CUDA tensor [N_seq, blocks_per_seq] for a paged cache: k_cache /
+    v_cache are then block pools [n_blocks, H_kv, page, D] (page a multiple of 64) and token t of
+    sequence s lives at block_table[s, t // page], token t % page.  Same bits as a contiguous cache.
     """
     import torch
 
     assert q.is_cuda and k_cache.is_cuda and v_cache.is_cuda, "attention requires CUDA tensors"
     R, H, D = q.shape
     n_seq, Hkv, cap, D2 = k_cache.shape
+    if block_table is not None:
+        assert block_table.dtype == torch.int32 and block_table.is_cuda and block_table.dim() == 2
+        assert block_table.stride(1) == 1
+        n_blocks, page = n_seq, cap
+        n_seq, cap = block_table.shape[0], block_table.shape[1] * page
     assert D2 == D and v_cache.shape == k_cache.shape, "q/k/v shape mismatch"
     assert k_cache.stride() == v_cache.stride(), "k and v caches must share strides"
     assert k_cache.stride(3) == 1 and q.stride(2) == 1, "unit stride along head_dim required"
@@ -105,6 +113,17 @@ def attention_decode(q, k_cache, v_cache, kv_lens, *, scale=None, row_tiles=None
     if workspace is None:
         nbytes = lib.dk_attention_workspace_size(n_tiles, rows_per_tile, H, Hkv, D, int(max_kv_len))
         workspace = _lib.workspace(nbytes, q.device, stream)
+    if block_table is not None:
+        rc = lib.dk_attention_paged_batch_invariant(
+            q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
+            k_cache.stride(1), k_cache.stride(2), n_blocks, page, block_table.data_ptr(), block_table.stride(0),
+            n_seq, block_table.shape[1], out.data_ptr(), out.stride(0), out.stride(1), lens_ptr, int(uniform),
+            tiles_ptr, int(n_tiles), R, H, Hkv, D, int(max_kv_len), float(scale), _lib.dtype_code(q.dtype),
+            workspace.data_ptr() if workspace is not None else None,
+            workspace.numel() if workspace is not None else 0, stream)
+        _lib.check(rc, "attention_paged_batch_invariant")
+        _lib.count_launch()
+        return out
     rc = lib.dk_attention_batch_invariant(
         q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
         k_cache.stride(1), k_cache.stride(2), n_seq, cap, out.data_ptr(), out.stride(0), out.stride(1),

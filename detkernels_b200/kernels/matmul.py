@@ -153,7 +153,7 @@ _EPILOGUES = {"store": _lib.DK_EPI_STORE, "residual": _lib.DK_EPI_RESIDUAL, "sil
 
 def matmul_fused(a, b, epilogue: str = "store", out=None, workspace=None, residual=None, q_cols: int = 0,
                  head_dim: int = 0, k_cache=None, v_cache=None, row_seq=None, row_pos=None, argmax_keys=None,
-                 norm_weight=None, norm_out=None, eps: float = 1e-6):
+                 norm_weight=None, norm_out=None, eps: float = 1e-6, block_table=None):
     """``matmul_batch_invariant`` (same K numerics) with the decoder's next element-wise op fused
     into the store; every step rounds where the unfused torch sequence rounds, so the result bits
     equal that sequence's.  Epilogues:
@@ -165,7 +165,9 @@ def matmul_fused(a, b, epilogue: str = "store", out=None, workspace=None, residu
     * ``"qkv_cache"``: the first ``q_cols`` columns are returned ([M, q_cols]); the next
       (N - q_cols)/2 are K, the last (N - q_cols)/2 are V, written into ``k_cache``/``v_cache``
       ([n_seq, H_kv, capacity, head_dim]) at sequence ``row_seq[m]`` (int32; None: m) and position
-      ``row_pos[m]`` (int32).
+      ``row_pos[m]`` (int32).  With ``block_table`` (int32 [n_seq, blocks_per_seq]) the caches are
+      block pools [n_blocks, H_kv, page, head_dim] and position p of sequence s goes to block
+      ``block_table[s, p // page]``, token ``p % page``.
     * ``"argmax"``: folds each row's first maximal column into ``argmax_keys`` (int64 [M] used as
       uint64, zero before the call; ``argmax_finish`` reads and re-zeroes them).  Logits are stored
       only when ``out`` is given.
@@ -179,7 +181,7 @@ def matmul_fused(a, b, epilogue: str = "store", out=None, workspace=None, residu
 
     M, K, N = _check_inputs(a, b, "matmul_fused")
     epi, out_cols = _epilogue_struct(epilogue, M, N, a.dtype, residual, q_cols, head_dim, k_cache, v_cache, row_seq,
-                                     row_pos, argmax_keys, norm_weight, norm_out, eps)
+                                     row_pos, argmax_keys, norm_weight, norm_out, eps, block_table)
     if out is None and epilogue != "argmax":
         out = torch.empty((M, out_cols), device=a.device, dtype=a.dtype)
     if out is not None:
@@ -202,7 +204,8 @@ def matmul_fused(a, b, epilogue: str = "store", out=None, workspace=None, residu
 
 
 def _epilogue_struct(epilogue, M, N, dtype, residual=None, q_cols=0, head_dim=0, k_cache=None, v_cache=None,
-                     row_seq=None, row_pos=None, argmax_keys=None, norm_weight=None, norm_out=None, eps=1e-6):
+                     row_seq=None, row_pos=None, argmax_keys=None, norm_weight=None, norm_out=None, eps=1e-6,
+                     block_table=None):
     """(dk_matmul_epilogue, output columns) for an [M, N] product of ``dtype`` with ``epilogue``."""
     import torch
 
@@ -239,6 +242,12 @@ def _epilogue_struct(epilogue, M, N, dtype, residual=None, q_cols=0, head_dim=0,
             k_cache.stride(2)
         epi.row_seq = row_seq.data_ptr() if row_seq is not None else None
         epi.row_pos = row_pos.data_ptr()
+        if block_table is not None:
+            assert block_table.dtype == torch.int32 and block_table.is_cuda and block_table.dim() == 2
+            assert block_table.stride(1) == 1
+            epi.block_table, epi.block_table_stride = block_table.data_ptr(), block_table.stride(0)
+            epi.page_size, epi.blocks_per_seq = k_cache.shape[2], block_table.shape[1]
+            epi.n_blocks = k_cache.shape[0]
         out_cols = q_cols
     elif epilogue == "argmax":
         assert argmax_keys is not None and argmax_keys.dtype == torch.int64 and argmax_keys.numel() >= M

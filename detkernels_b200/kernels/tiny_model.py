@@ -183,7 +183,8 @@ class TinyModel:
         logits = matmul(rmsnorm(x, self.norm_f_w, cfg.eps), self.w_lm_head)
         return logits, new_kv_cache
 
-    def generate(self, prompt_token_ids, n_steps: int, kernel_set: str, *, tp: int = 1, group=None):
+    def generate(self, prompt_token_ids, n_steps: int, kernel_set: str, *, tp: int = 1, group=None,
+                 kv_page_size: Optional[int] = None):
         """Greedy decoding.  prompt_token_ids: (B,) int64 start tokens (the
         reference's form) or a list of B token-id lists (ragged prompts).
         Returns (B, n_steps) generated token ids.
@@ -191,10 +192,15 @@ class TinyModel:
         tp / group (keyword-only, invariant kernel set on CUDA): decode with every layer split
         over ``tp`` tensor-parallel ranks -- the ranks of ``group`` (a torch.distributed group of
         ``tp`` processes, each calling generate with the same prompts), or, with ``group=None``,
-        all ``tp`` ranks in this process on this model's GPU.  The tokens equal TP=1's bit for bit."""
+        all ``tp`` ranks in this process on this model's GPU.  The tokens equal TP=1's bit for bit.
+        kv_page_size (keyword-only, invariant set on CUDA): keep the KV cache in blocks of that many
+        tokens (a multiple of 64) behind a block table; the tokens are the same bits."""
         import torch
 
         ragged = isinstance(prompt_token_ids, (list, tuple))
+        if kv_page_size is not None and (kernel_set != "batch_invariant" or not str(self.device).startswith("cuda")
+                                         or tp != 1 or group is not None):
+            raise ValueError("a paged KV cache is served by the one-GPU batch_invariant engine on CUDA")
         if tp != 1 or group is not None:
             if kernel_set != "batch_invariant" or not str(self.device).startswith("cuda"):
                 raise ValueError("tensor-parallel decoding runs the batch_invariant kernel set on CUDA")
@@ -206,7 +212,7 @@ class TinyModel:
             # with numpy); a (B,) tensor becomes B one-token prompts
             prompts = (list(prompt_token_ids) if ragged else [[int(t)] for t in prompt_token_ids.tolist()])
             cap = max(len(p) for p in prompts) + n_steps
-            eng = self.engine(len(prompts), cap)
+            eng = self.engine(len(prompts), cap, page_size=kv_page_size)
             return eng.generate(prompts, n_steps)
         if ragged:
             return self._generate_ragged_eager(prompt_token_ids, n_steps, kernel_set)
@@ -252,14 +258,48 @@ class TinyModel:
         self._engines[("tp", tp, gid, max_batch, max_seq_len, use_graph)] = eng
         return eng
 
-    def engine(self, max_batch: int, max_seq_len: int, use_graph: bool = True) -> "DecodeEngine":
-        """A cached DecodeEngine whose capacity covers (max_batch, max_seq_len)."""
-        for (kind, _, _, b, s, g), eng in self._engines.items():
-            if kind == "dp" and b >= max_batch and s >= max_seq_len and g == use_graph:
+    def engine(self, max_batch: int, max_seq_len: int, use_graph: bool = True,
+               page_size: Optional[int] = None) -> "DecodeEngine":
+        """A cached DecodeEngine whose capacity covers (max_batch, max_seq_len); page_size: a paged
+        KV cache of blocks of that many tokens (a multiple of 64) instead of one slab per sequence."""
+        kind = "dp" if page_size is None else ("paged", int(page_size))
+        for (k, _, _, b, s, g), eng in self._engines.items():
+            if k == kind and b >= max_batch and s >= max_seq_len and g == use_graph:
                 return eng
-        eng = DecodeEngine(self, max_batch, max_seq_len, use_graph=use_graph)
-        self._engines[("dp", 1, None, max_batch, max_seq_len, use_graph)] = eng
+        eng = DecodeEngine(self, max_batch, max_seq_len, use_graph=use_graph, page_size=page_size)
+        self._engines[(kind, 1, None, max_batch, max_seq_len, use_graph)] = eng
         return eng
+
+
+class BlockAllocator:
+    """Host-side owner of a paged KV pool's blocks.  Block 0 is never handed out: padding rows
+    and unused table entries point at it.  ``assign`` starts from a free pool and gives slot b
+    ceil(tokens[b] / page) blocks in a seeded shuffled order, so neighbouring sequences do not
+    get neighbouring blocks; a request the pool cannot hold raises RuntimeError."""
+
+    def __init__(self, n_blocks: int, max_slots: int, blocks_per_seq: int, seed: int = 0):
+        import numpy as np
+
+        if n_blocks < 2:
+            raise ValueError("a paged pool needs at least two blocks")
+        self.n_blocks, self.max_slots, self.blocks_per_seq = n_blocks, max_slots, blocks_per_seq
+        self.order = np.random.default_rng(seed).permutation(np.arange(1, n_blocks, dtype=np.int32))
+
+    def assign(self, tokens, page):
+        import numpy as np
+
+        need = [-(-int(t) // page) for t in tokens]
+        if len(need) > self.max_slots or any(n > self.blocks_per_seq for n in need):
+            raise ValueError("more sequences or tokens than the engine was built for")
+        if sum(need) > self.n_blocks - 1:
+            raise RuntimeError("KV block pool exhausted: %d blocks needed, %d available"
+                               % (sum(need), self.n_blocks - 1))
+        table = np.zeros((self.max_slots, self.blocks_per_seq), dtype=np.int32)
+        pos = 0
+        for b, n in enumerate(need):
+            table[b, :n] = self.order[pos:pos + n]
+            pos += n
+        return table
 
 
 class DecodeEngine:
@@ -273,7 +313,8 @@ class DecodeEngine:
 
     MAX_GRAPHS = 8   # captured decode graphs kept per engine
 
-    def __init__(self, model: TinyModel, max_batch: int, max_seq_len: int, use_graph: bool = True):
+    def __init__(self, model: TinyModel, max_batch: int, max_seq_len: int, use_graph: bool = True,
+                 page_size: Optional[int] = None, n_blocks: Optional[int] = None):
         import torch
 
         from detkernels_b200 import _lib
@@ -292,8 +333,21 @@ class DecodeEngine:
         self.use_graph = use_graph
         self.layers = model.fused_layer_weights()
         dev, dt = self.device, self.dtype
-        self.k_cache = [torch.zeros(self.B, self.Hkv, self.S, self.D, device=dev, dtype=dt)
-                        for _ in range(cfg.num_layers)]
+        self.page_size = page_size
+        self.block_table = None
+        if page_size is None:
+            self.k_cache = [torch.zeros(self.B, self.Hkv, self.S, self.D, device=dev, dtype=dt)
+                            for _ in range(cfg.num_layers)]
+        else:
+            if page_size <= 0 or page_size % 64:
+                raise ValueError("page_size must be a positive multiple of 64, got %r" % (page_size,))
+            per_seq = -(-self.S // page_size)
+            if n_blocks is None:
+                n_blocks = 1 + self.B * per_seq      # block 0 + every slot at full capacity
+            self.allocator = BlockAllocator(int(n_blocks), self.B, per_seq)
+            self.k_cache = [torch.zeros(int(n_blocks), self.Hkv, page_size, self.D, device=dev, dtype=dt)
+                            for _ in range(cfg.num_layers)]
+            self.block_table = torch.zeros(self.B, per_seq, dtype=torch.int32, device=dev)
         self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
         # decode-step state
         self.tokens = torch.zeros(self.B, dtype=torch.long, device=dev)
@@ -333,11 +387,11 @@ class DecodeEngine:
         R = x.shape[0]
         H, D = self.H, self.D
         q = self._mm(xn, layer["w_qkv"], "qkv_cache", q_cols=H * D, head_dim=D, k_cache=self.k_cache[li],
-                     v_cache=self.v_cache[li], row_seq=write_seq, row_pos=write_pos)
+                     v_cache=self.v_cache[li], row_seq=write_seq, row_pos=write_pos, block_table=self.block_table)
         if events is not None:
             events[0].record()
         attn = attention_decode(q.view(R, H, D), self.k_cache[li], self.v_cache[li], q_lens, row_tiles=row_tiles,
-                                max_kv_len=max_len, workspace=attn_ws)
+                                max_kv_len=max_len, workspace=attn_ws, block_table=self.block_table)
         if events is not None:
             events[1].record()
         xn = torch.empty_like(x)
@@ -393,6 +447,7 @@ class DecodeEngine:
         plan["rows32"] = plan["rows"].to(torch.int32)
         plan["pos32"] = plan["pos"].to(torch.int32)
         plan["B"] = B
+        plan["lens_host"] = lens
         plan["max_len"] = int(lens.max())
         plan["h2d_bytes"] = sum(v.numel() * v.element_size() for v in host.values())
         lib = self._lib.load()
@@ -406,9 +461,23 @@ class DecodeEngine:
         plan["gemm_ws"] = torch.zeros(max(g_ws, 1), dtype=torch.uint8, device=dev)
         return plan
 
+    def _reserve_blocks(self, plan, n_steps):
+        """Paged cache: blocks for every prompt plus n_steps tokens (from a fresh pool; the slots
+        past the batch and unused table entries point at block 0, which the padding rows of a
+        decode step may write)."""
+        if self.block_table is None:
+            return
+        import torch
+
+        lens = plan["lens_host"]
+        table = self.allocator.assign([int(L) + n_steps for L in lens], self.page_size)
+        self.block_table.copy_(torch.from_numpy(table).pin_memory(), non_blocking=True)
+
     def prefill(self, plan):
         """Run a planned prefill; returns logits of each prompt's last token and
         leaves the cache and kv_lens ready for decoding."""
+        if self.block_table is not None and plan.get("reserved") is None:
+            self._reserve_blocks(plan, 1)
         saved = self.gemm_ws
         self.gemm_ws = plan["gemm_ws"]
         try:
@@ -525,6 +594,9 @@ class DecodeEngine:
             return torch.empty((B, 0), dtype=torch.long, device=self.device)
         if plan["max_len"] + n_steps > self.S:
             raise ValueError("prompt + n_steps exceeds the engine's max_seq_len")
+        if self.block_table is not None:
+            self._reserve_blocks(plan, n_steps)
+            plan["reserved"] = n_steps
         first = self._prefill_tokens(plan)
         self.tokens.zero_()
         self.tokens[:B] = first

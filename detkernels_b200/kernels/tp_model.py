@@ -158,6 +158,7 @@ class TPDecodeEngine(DecodeEngine):
         self.H, self.Hkv, self.D = lay.Hl, lay.Hkvl, lay.D
         self.h = cfg.hidden_size
         self.use_graph = use_graph
+        self.page_size, self.block_table = None, None   # the shards keep contiguous caches
         self.shards: List[_Shard] = [_Shard(model, lay, r, self.B, self.S, self.device) for r in local]
         self.norms = [{"norm1_w": L["norm1_w"], "norm2_w": L["norm2_w"]} for L in model.layers]
         self.layers = self.norms   # the base class reads layers[li]["norm1_w"]

@@ -58,8 +58,9 @@ extern "C" {
 
 /* ---- library / device queries ---- */
 /* Layout version of this header's structs and signatures; dk_abi_version() of a library built from it
- * returns the same number.  2: dk_matmul_epilogue gained the DK_EPI_RESIDUAL_RMSNORM fields. */
-#define DK_ABI_VERSION 2
+ * returns the same number.  2: dk_matmul_epilogue gained the DK_EPI_RESIDUAL_RMSNORM fields.
+ * 3: dk_matmul_epilogue gained the paged-KV fields (block_table ... n_blocks). */
+#define DK_ABI_VERSION 3
 int dk_abi_version(void);
 /* Message for the last non-zero return code on the calling host thread. */
 const char* dk_last_error(void);
@@ -186,6 +187,16 @@ typedef struct dk_matmul_epilogue {
   void* norm_out;          /* [M, N] rows norm_ld apart, dtype of C */
   int64_t norm_ld;
   float norm_eps;
+  /* DK_EPI_QKV_CACHE into a paged cache (block_table non-NULL): k_cache / v_cache are block pools
+   * [n_blocks, heads, page_size, head_dim] (cache_stride_seq = the block stride), and position pos of
+   * sequence s goes to block block_table[s * block_table_stride + pos / page_size], token pos %
+   * page_size.  A position past blocks_per_seq blocks or an entry outside [0, n_blocks) is recorded as
+   * DK_ERR_DEVICE_CHECK and not stored. */
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  int32_t page_size;
+  int32_t blocks_per_seq;
+  int64_t n_blocks;
 } dk_matmul_epilogue;
 
 /* dk_matmul_batch_invariant followed by the epilogue `epi` (same K numerics; NULL epi = DK_EPI_STORE).
@@ -243,6 +254,27 @@ int dk_attention_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_
                                  int32_t n_rows, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
                                  int32_t max_kv_len, float scale, int dtype, void* workspace,
                                  size_t workspace_bytes, void* stream);
+
+/* Decode attention over a paged KV cache: the arithmetic, arguments and bits of
+ * dk_attention_batch_invariant, with the K/V cache given as block pools k_pool / v_pool
+ * [n_blocks, n_kv_heads, page_size, head_dim] (element strides pool_stride_block, pool_stride_head,
+ * pool_stride_tok; unit d stride) and a block table: token t of KV sequence s is token t % page_size
+ * of block block_table[s * block_table_stride + t / page_size] (device int32 [kv_n_seq][...], at least
+ * blocks_per_seq entries per row).  page_size must be a multiple of 64; kv lengths may reach
+ * blocks_per_seq * page_size.  A table entry outside [0, n_blocks) is recorded as DK_ERR_DEVICE_CHECK
+ * (detail 0x212).  Workspace as dk_attention_workspace_size.  No counterpart in the reference: its
+ * cache is one contiguous tensor grown by torch.cat (kernels/tiny_model.py:119-125) and it lists
+ * paging as a simplification (kernels/attention.py:35-40). */
+int dk_attention_paged_batch_invariant(const void* q, int64_t q_stride_row, int64_t q_stride_head,
+                                       const void* k_pool, const void* v_pool, int64_t pool_stride_block,
+                                       int64_t pool_stride_head, int64_t pool_stride_tok, int64_t n_blocks,
+                                       int32_t page_size, const int32_t* block_table, int64_t block_table_stride,
+                                       int64_t kv_n_seq, int32_t blocks_per_seq, void* out, int64_t out_stride_row,
+                                       int64_t out_stride_head, const int32_t* kv_lens, int32_t uniform_kv_len,
+                                       const int32_t* row_tiles, int32_t n_tiles, int32_t n_rows,
+                                       int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_kv_len,
+                                       float scale, int dtype, void* workspace, size_t workspace_bytes,
+                                       void* stream);
 
 /* Scratch bytes dk_attention_batch_variant needs. */
 size_t dk_attention_variant_workspace_size(int32_t batch, int32_t n_heads, int32_t head_dim);

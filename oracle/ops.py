@@ -171,13 +171,18 @@ class TinyModelOracle:
     def empty_caches(self, batch):
         return [[_SeqCache(self.Hkv, self.D) for _ in range(batch)] for _ in self.w["layers"]]
 
-    def generate(self, prompts, n_steps, margins=None):
+    def generate(self, prompts, n_steps, margins=None, follow=None, regrets=None):
         """Greedy decode; prompts: list of token lists. Returns (tokens [B, n_steps], last logits).
         margins (optional list): receives per row the top-1 minus top-2 logit of every generated
-        token's step, so a caller can tell a near-tie from a real disagreement."""
+        token's step, so a caller can tell a near-tie from a real disagreement.
+        follow (optional [B][n_steps] tokens, teacher forcing): the sequence continues with these
+        tokens instead of the oracle's choice (the oracle's argmax is still returned), and regrets
+        (optional list) receives per row max(logits) - logits[follow token] at every step."""
         B = len(prompts)
         if margins is not None:
             margins[:] = [[] for _ in range(B)]
+        if regrets is not None:
+            regrets[:] = [[] for _ in range(B)]
         caches = self.empty_caches(B)
         maxp = max(len(p) for p in prompts)
         # feed prompts token by token; a row whose prompt is exhausted starts generating
@@ -200,8 +205,15 @@ class TinyModelOracle:
                     cur[b] = prompts[b][pos[b]]
                 else:
                     nxt = int(np.argmax(logits[i]))
-                    out[b].append(nxt)
-                    cur[b] = nxt
+                    if follow is not None:
+                        forced = int(follow[b][len(out[b])])
+                        if regrets is not None:
+                            regrets[b].append(float(logits[i][nxt] - logits[i][forced]))
+                        out[b].append(nxt)
+                        cur[b] = forced
+                    else:
+                        out[b].append(nxt)
+                        cur[b] = nxt
                     if margins is not None:
                         top2 = np.partition(logits[i], -2)[-2:]
                         margins[b].append(float(top2[1] - top2[0]))

@@ -46,7 +46,7 @@ def test_python_binding_covers_the_header():
 
 def test_host_side_validation_without_a_gpu(lib):
     from detkernels_b200 import _lib
-    assert lib.dk_abi_version() == _lib.ABI_VERSION == 2
+    assert lib.dk_abi_version() == _lib.ABI_VERSION == 3
     # unsupported dtype code
     rc = lib.dk_rmsnorm_batch_invariant(None, 0, None, None, 0, 4, 8, 7, 0, 1e-6, None)
     assert rc == _lib.DK_ERR_UNSUPPORTED

@@ -1,0 +1,93 @@
+"""The CTA-pair GEMM (tcgen05.mma.cta_group::2, 256 weight columns x 128 tokens per
+pair) against the one-CTA GEMM: the same bits on the same shapes, for plain stores,
+split-K schedules and fused epilogues.  A test hook that is not part of the public
+header forces either kernel."""
+import ctypes
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(300, 512, 1024), (1000, 4096, 4096), (2048, 11008, 4096), (129, 256, 64), (513, 1000, 200),
+          (4096, 1024, 2816), (257, 3072, 1024), (7, 768, 96)]
+
+
+def _force(mode):
+    from detkernels_b200 import _lib
+    fn = _lib.load().dk_matmul_pair_schedule_for_test
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_int]
+    return fn(mode)
+
+
+@pytest.fixture
+def restore_schedule():
+    yield
+    _force(0)
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_pair_kernel_equals_one_cta_kernel(dev, restore_schedule, M, N, K):
+    import torch
+
+    from detkernels_b200.kernels.matmul import matmul_batch_invariant
+    g = torch.Generator(device=dev).manual_seed(M + N + K)
+    a = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    b = (0.02 * torch.randn(K, N, device=dev, generator=g)).to(torch.bfloat16)
+    _force(1)
+    want = matmul_batch_invariant(a, b)
+    _force(2)
+    got = matmul_batch_invariant(a, b)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    # f16 too
+    a16, b16 = a.to(torch.float16), b.to(torch.float16)
+    _force(1)
+    want16 = matmul_batch_invariant(a16, b16)
+    _force(2)
+    assert torch.equal(matmul_batch_invariant(a16, b16), want16)
+
+
+@pytest.mark.parametrize("epilogue", ["residual_rmsnorm", "silu_mul", "argmax", "silu"])
+def test_pair_kernel_fused_epilogues(dev, restore_schedule, epilogue):
+    import torch
+
+    from detkernels_b200.kernels.matmul import matmul_fused
+    g = torch.Generator(device=dev).manual_seed(9)
+    M, K, N = 700, 1024, 2048
+    a = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    b = (0.02 * torch.randn(K, N, device=dev, generator=g)).to(torch.bfloat16)
+    r = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(N, device=dev, generator=g)).to(torch.bfloat16)
+    outs = []
+    for mode in (1, 2):
+        _force(mode)
+        if epilogue == "residual_rmsnorm":
+            nrm = torch.empty_like(r)
+            y = matmul_fused(a, b, "residual_rmsnorm", residual=r, norm_weight=w, norm_out=nrm)
+            outs.append((y, nrm))
+        elif epilogue == "argmax":
+            keys = torch.zeros(M, dtype=torch.int64, device=dev)
+            matmul_fused(a, b, "argmax", argmax_keys=keys)
+            outs.append((keys,))
+        else:
+            outs.append((matmul_fused(a, b, epilogue),))
+    torch.cuda.synchronize()
+    for x, y in zip(*outs):
+        assert torch.equal(x, y)
+
+
+def test_pair_kernel_rows_equal_one_cta_rows_at_other_m(dev, restore_schedule):
+    """Row 0 of a 2048-token product on the pair kernel equals the same row at M = 1, 64 and
+    256 on the one-CTA kernel."""
+    import torch
+
+    from detkernels_b200.kernels.matmul import matmul_batch_invariant
+    _force(2)
+    g = torch.Generator(device=dev).manual_seed(3)
+    a = torch.randn(2048, 4096, device=dev, generator=g).to(torch.bfloat16)
+    b = (0.02 * torch.randn(4096, 4096, device=dev, generator=g)).to(torch.bfloat16)
+    big = matmul_batch_invariant(a, b)
+    _force(1)
+    for m in (1, 64, 256):
+        assert torch.equal(matmul_batch_invariant(a[:m].contiguous(), b)[0], big[0]), m

@@ -9,9 +9,12 @@
   8192 (32 splits of 256 merged online) against the f32 oracle.
 * TinyModel: the benchmark model (4 layers, d 1024, 16 x 64, SwiGLU 2816, vocab
   32000, bf16) decoding 128 greedy tokens for the tracked 32-token prompt and 7
-  ragged prompts of 16-512 tokens: every row equals the oracle's tokens up to
-  its first near-tie (an oracle step whose top-2 logits are within
-  NEAR_TIE), and the margins at such steps are reported.
+  ragged prompts of 16-512 tokens.  The oracle is teacher-forced with the
+  kernel's tokens: at every one of the 1024 steps the kernel's token must be
+  within NEAR_TIE of the oracle's largest logit (its argmax up to a near-tie),
+  so each row equals the free-running oracle up to its first near-tie.  With
+  32000 bf16 logits such ties are common (margins of 0 or 1 ulp were seen at the
+  first difference of every row), so rows may part after one.
 """
 import numpy as np
 import pytest
@@ -126,20 +129,13 @@ def test_tinymodel_128_token_decode_matches_the_oracle_to_the_first_near_tie(dev
     w = {"embed": f(model.embed), "layers": [{kk: f(vv) for kk, vv in L.items()} for L in model.layers],
          "norm_f_w": f(model.norm_f_w), "w_lm_head": f(model.w_lm_head)}
     orc = oracle.TinyModelOracle(w, 16, 16, 64, mlp="swiglu", dtype="bfloat16")
-    margins = []
-    want, _ = orc.generate(prompts, 128, margins=margins)
-    report = []
-    for b in range(len(prompts)):
-        diff = np.nonzero(got[b] != want[b])[0]
-        if diff.size == 0:
-            report.append((b, 128, None))
-            continue
-        t = int(diff[0])
-        report.append((b, t, margins[b][t]))
-        assert margins[b][t] < NEAR_TIE, "row %d differs at token %d where the oracle's top-2 margin is %g: %s" % (
-            b, t, margins[b][t], report)
-    matched = sum(r[1] for r in report)
-    print("tokens matching the oracle before the first near-tie: %d of %d; (row, first difference, margin): %s"
-          % (matched, 128 * len(prompts), report))
-    # the tracked row and most of the batch must agree for long stretches, not only to the first tie
-    assert matched >= 0.5 * 128 * len(prompts), report
+    regrets = []
+    want, _ = orc.generate(prompts, 128, follow=got, regrets=regrets)
+    regrets = np.asarray(regrets)
+    agree = got == want
+    first = [int(np.argmin(np.append(row, False))) for row in agree]
+    print("kernel token == oracle argmax at %d of %d teacher-forced steps; worst regret %g; first difference "
+          "per row %s with regrets %s" % (int(agree.sum()), agree.size, float(regrets.max()), first,
+                                          [float(regrets[b, t]) if t < 128 else None for b, t in enumerate(first)]))
+    assert regrets.max() < NEAR_TIE, (regrets.max(), np.argwhere(regrets >= NEAR_TIE)[:10])
+    assert agree[0, :first[0]].all() and first[0] >= 1
