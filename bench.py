@@ -703,8 +703,9 @@ def main(argv=None):
     ap.add_argument("--rmsnorm-only", action="store_true", help="run and print only the RMSNorm roofline section")
     ap.add_argument("--gemm-only", default=None, metavar="M,N",
                     help="run and print only matmul_batch_invariant [M,4096] x [4096,N] against cuBLAS (profiling)")
-    ap.add_argument("--gemm-kernel", choices=["auto", "one", "pair"], default="auto",
-                    help="with --gemm-only: the planner's kernel, the one-CTA kernel or the CTA-pair kernel")
+    ap.add_argument("--gemm-kernel", choices=["auto", "one", "pair", "wide"], default="auto",
+                    help="with --gemm-only: the planner's kernel, the one-CTA kernel, the CTA-pair kernel "
+                         "(256 x 128 tiles) or the wide CTA-pair kernel (256 x 256 tiles)")
     ap.add_argument("--tp", type=int, default=1, choices=[1, 2, 4, 8],
                     help="tensor-parallel decode over the torchrun ranks (needs --nproc-per-node TP)")
     ap.add_argument("--new-tokens", type=int, default=NEW_TOKENS,
@@ -721,7 +722,7 @@ def main(argv=None):
             from detkernels_b200 import _lib
             hook = _lib.load().dk_matmul_pair_schedule_for_test   # not in the public header
             hook.restype, hook.argtypes = ctypes.c_int, [ctypes.c_int]
-            hook(1 if args.gemm_kernel == "one" else 2)
+            hook({"one": 1, "pair": 2, "wide": 3}[args.gemm_kernel])
         global GEMM_SHAPES
         GEMM_SHAPES = [(m, n)]
         print(json.dumps({"gemm_vs_cublas": gemm_vs_cublas(iters=5)}), flush=True)

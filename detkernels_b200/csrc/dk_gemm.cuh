@@ -122,6 +122,7 @@ struct Params {
   void* c;
   int64_t ldc;
   float* ws;       // SPLIT: subtree sums [8/g][M][N]; PARTIAL: [M][N]; ATOMIC: [M][N]
+  float* stash;    // wide kernel, 8-slice units: a parking place per CTA for the tree's left half
 };
 
 // Detail codes recorded with a timeout (which wait expired).

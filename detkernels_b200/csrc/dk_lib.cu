@@ -16,6 +16,7 @@
 #include "dk_rmsnorm.cuh"
 #include "dk_gemm.cuh"
 #include "dk_gemm2.cuh"
+#include "dk_gemm_wide.cuh"
 #include "dk_attention.cuh"
 #include "dk_attention_variant.cuh"
 #include "dk_gdn.cuh"
@@ -271,23 +272,28 @@ int slice_len_for(int64_t K, int n_slices) {
 struct GemmPlan {
   int mode;
   int group;
-  bool pair;           // CTA-pair kernel (n_tiles then counts 256-column pair tiles)
+  int kernel;          // 0 one-CTA, 1 CTA pair (256-column tiles), 2 wide CTA pair (256 x 256 tiles)
   int n_tiles, m_tiles;
   size_t ws_bytes;     // workspace bytes this plan needs
   size_t counters_off; // byte offset of the counters region
   size_t partials_off; // byte offset of the partials region
+  bool stash;          // the wide kernel with 8-slice units parks the tree's left half in the workspace
+  size_t stash_off;    // byte offset of that stash
 };
 
 // Schedule choice (never changes the arithmetic): slices per work unit.  A
 // small cost model -- per-SM streaming of the unit's operand tiles in waves,
 // plus the L2 round trip of the f32 slice partials when slices are spread
 // over CTAs -- picks the cheapest of 8 (FOLD), 4, 2, 1 (SPLIT).
-int pick_group(int64_t M, int64_t N, int64_t K, int64_t tiles, int sms) {
-#ifdef DK_GEMM_FORCE_GROUP
-  (void)M; (void)N; (void)K; (void)tiles; (void)sms;
-  return DK_GEMM_FORCE_GROUP;
-#endif
+// Slices per work unit forced by the test hook dk_matmul_pair_schedule_for_test (0: the cost model).
+int g_group_override = 0;
+
+int pick_group(int64_t M, int64_t N, int64_t K, int64_t tiles, int sms, int kernel) {
+  if (g_group_override) return g_group_override;
   const int a_rows = (M <= dk::gemm::kTileM) ? static_cast<int>(ceil_div(M, 8) * 8) : dk::gemm::kTileM;
+  const int stage_bytes = (kernel == 2) ? dk::gemm::kWideStageBytes
+                          : (kernel == 1) ? dk::gemm::kPairStageBytes
+                                          : dk::gemm::stage_bytes_for(a_rows);
   const double kSmBytesPerUs = 100e3;   // sustained TMA bytes per SM per microsecond
   const double kL2BytesPerUs = 10e6;    // L2 bytes per microsecond for the partial round trip
   const int64_t kb_per_slice = ceil_div(slice_len_for(K, dk::gemm::kSlices), dk::gemm::kBK);
@@ -296,7 +302,7 @@ int pick_group(int64_t M, int64_t N, int64_t K, int64_t tiles, int sms) {
   for (int g = dk::gemm::kSlices; g >= 1; g /= 2) {
     const int64_t units = tiles * (dk::gemm::kSlices / g);
     const int64_t waves = ceil_div(units, sms);
-    const double load = static_cast<double>(waves) * g * kb_per_slice * dk::gemm::stage_bytes_for(a_rows) / kSmBytesPerUs;
+    const double load = static_cast<double>(waves) * g * kb_per_slice * stage_bytes / kSmBytesPerUs;
     // each unit writes one subtree sum; the last arriver reads them back
     const double part = (g < dk::gemm::kSlices) ? 2.0 * (dk::gemm::kSlices / g) * M * N * 4 / kL2BytesPerUs : 0.0;
     const double t = load + part;
@@ -309,33 +315,46 @@ int pick_group(int64_t M, int64_t N, int64_t K, int64_t tiles, int sms) {
 }
 
 // Which GEMM kernel runs an invariant call (never changes the arithmetic): 0 = the planner's
-// choice, 1 = always the one-CTA kernel, 2 = always the CTA-pair kernel.  Only the test hook
-// dk_matmul_pair_schedule_for_test sets it.
+// choice, 1 = always the one-CTA kernel, 2 = always the CTA-pair kernel, 3 = always the wide
+// CTA-pair kernel.  Only the test hook dk_matmul_pair_schedule_for_test sets it.
 int g_pair_override = 0;
 
-// The CTA-pair kernel moves 24 KB per SM per 128 x 128 x 64 of work instead of 32 KB, but
-// measured on B200 it is not yet faster than the one-CTA kernel (M = 2048, N = 4096: 147 vs
-// 129 us), so the planner keeps the one-CTA kernel; the pair kernel runs when forced.
-bool use_pair_kernel(int64_t M, int64_t N) {
-  (void)M;
+// The CTA-pair kernel with 256 x 128 tiles moves 24 KB per SM per 128 x 128 x 64 of work instead
+// of 32 KB, but measured on B200 it is not faster than the one-CTA kernel (M = 2048, N = 4096:
+// 147 vs 129 us); it runs only when forced.  The wide kernel (256 x 256 tiles, 16 KB per SM per
+// 128 x 128 x 64) runs when the token count fills its 256-token tiles.
+int pick_kernel(int64_t M, int64_t N) {
   (void)N;
-  return g_pair_override == 2;
+  if (g_pair_override == 1) return 0;
+  if (g_pair_override == 2) return 1;
+  if (g_pair_override == 3) return 2;
+  return (M > dk::gemm::kTileM) ? 2 : 0;
 }
 
 GemmPlan plan_invariant(int64_t M, int64_t N, int64_t K, int sms) {
   GemmPlan pl{};
-  pl.pair = use_pair_kernel(M, N);
-  pl.n_tiles = static_cast<int>(ceil_div(N, pl.pair ? dk::gemm::kPairTileN : dk::gemm::kTileN));
-  pl.m_tiles = static_cast<int>(ceil_div(M, dk::gemm::kTileM));
-  const int64_t tiles = static_cast<int64_t>(pl.n_tiles) * pl.m_tiles * (pl.pair ? 2 : 1);   // in CTAs
-  const int group = pick_group(M, N, K, tiles, sms);
+  pl.kernel = pick_kernel(M, N);
+  const int tile_n = pl.kernel ? dk::gemm::kPairTileN : dk::gemm::kTileN;
+  const int tile_m = (pl.kernel == 2) ? dk::gemm::kWideTileM : dk::gemm::kTileM;
+  pl.n_tiles = static_cast<int>(ceil_div(N, tile_n));
+  pl.m_tiles = static_cast<int>(ceil_div(M, tile_m));
+  const int64_t tiles = static_cast<int64_t>(pl.n_tiles) * pl.m_tiles * (pl.kernel ? 2 : 1);   // in CTAs
+  const int group = pick_group(M, N, K, tiles, sms, pl.kernel);
   pl.group = group;
   pl.mode = (group == dk::gemm::kSlices) ? dk::gemm::FOLD : dk::gemm::SPLIT;
+  size_t end = 0;
   if (pl.mode == dk::gemm::SPLIT) {
     pl.counters_off = 0;
     pl.partials_off = kCounterBytes;
-    pl.ws_bytes = pl.partials_off + sizeof(float) * static_cast<size_t>(dk::gemm::kSlices / group) * M * N;
+    end = pl.partials_off + sizeof(float) * static_cast<size_t>(dk::gemm::kSlices / group) * M * N;
   }
+  if (pl.kernel == 2 && group == dk::gemm::kSlices) {
+    // one stash per CTA the launch can hold resident (at most one CTA per SM)
+    pl.stash = true;
+    pl.stash_off = (end + 255) / 256 * 256;
+    end = pl.stash_off + sizeof(float) * static_cast<size_t>(dk::gemm::kWideStashFloats) * sms;
+  }
+  pl.ws_bytes = end;
   return pl;
 }
 
@@ -443,10 +462,54 @@ cudaError_t launch_pair(const CUtensorMap& tmB, const CUtensorMap& tmA, const dk
   return cudaLaunchKernelEx(&cfg, fn, tmB, tmA, p);
 }
 
+// The wide kernel's launch: clusters of 2, as many pairs as can be resident at once (at most
+// one CTA per SM, which the stash is sized for).  Its register split (setmaxnreg) is exact only
+// for kWideLaunchRegs registers per thread, so a build with another count is refused.
+template <typename T, int FMT, bool FOLDK>
+cudaError_t launch_wide(const CUtensorMap& tmB, const CUtensorMap& tmA, const dk::gemm::Params& p, int64_t units,
+                        cudaStream_t st, int* rc) {
+  auto fn = dk::gemm::gemm_wide_kernel<T, FMT, FOLDK>;
+  static bool done[kMaxDevices] = {};
+  static int max_pairs[kMaxDevices] = {};
+  *rc = ensure_smem(fn, dk::gemm::kSmemBytes, done);
+  if (*rc) return cudaSuccess;
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess || fa.numRegs != dk::gemm::kWideLaunchRegs) {
+    *rc = fail(DK_ERR_UNSUPPORTED, "wide GEMM built with %d registers per thread, %d expected", fa.numRegs,
+               dk::gemm::kWideLaunchRegs);
+    return cudaSuccess;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(dk::gemm::kWideThreads);
+  cfg.dynamicSmemBytes = dk::gemm::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const int dev = current_device();
+  int pairs = (dev >= 0 && dev < kMaxDevices) ? max_pairs[dev] : 0;
+  if (pairs <= 0) {
+    cfg.gridDim = dim3(2 * 64);
+    if (cudaOccupancyMaxActiveClusters(&pairs, fn, &cfg) != cudaSuccess || pairs <= 0) pairs = sm_count(dev) / 2;
+    if (pairs > sm_count(dev) / 2) pairs = sm_count(dev) / 2;
+    if (dev >= 0 && dev < kMaxDevices) max_pairs[dev] = pairs;
+  }
+  const int64_t n = units < pairs ? units : pairs;
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * n));
+  return cudaLaunchKernelEx(&cfg, fn, tmB, tmA, p);
+}
+
 int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ldb, dk::gemm::Params p,
                 cudaStream_t st, const char* what, const NormSpec* norm = nullptr) {
-  p.a_rows = p.pair ? dk::gemm::kPairRows
-                    : ((p.m_tiles == 1) ? static_cast<int>(ceil_div(p.M, 8) * 8) : dk::gemm::kTileM);
+  p.a_rows = (p.pair == 2) ? dk::gemm::kWideRows
+             : p.pair      ? dk::gemm::kPairRows
+                           : ((p.m_tiles == 1) ? static_cast<int>(ceil_div(p.M, 8) * 8) : dk::gemm::kTileM);
   const int64_t k_mem = p.k_extent > 0 ? p.k_extent : p.K;
   CUtensorMap tmB, tmA;
   const uint64_t dimsB[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(k_mem)};
@@ -468,7 +531,16 @@ int gemm_launch(int dtype, const void* a, int64_t lda, const void* b, int64_t ld
   if (grid <= 0) return DK_OK;
   cudaError_t e;
   const bool fold = (p.mode == dk::gemm::FOLD);
-  if (p.pair) {
+  if (p.pair == 2) {
+    int lrc = DK_OK;
+    if (dtype == DK_BF16)
+      e = fold ? launch_wide<__nv_bfloat16, 1, true>(tmB, tmA, p, units, st, &lrc)
+               : launch_wide<__nv_bfloat16, 1, false>(tmB, tmA, p, units, st, &lrc);
+    else
+      e = fold ? launch_wide<__half, 0, true>(tmB, tmA, p, units, st, &lrc)
+               : launch_wide<__half, 0, false>(tmB, tmA, p, units, st, &lrc);
+    if (lrc) return lrc;
+  } else if (p.pair) {
     int lrc = DK_OK;
     if (dtype == DK_BF16)
       e = fold ? launch_pair<__nv_bfloat16, 1, true>(tmB, tmA, p, units, st, &lrc)
@@ -863,16 +935,19 @@ int dk_matmul_batch_invariant_ex(const void* a, int64_t lda, const void* b, int6
   p.n_tiles = pl.n_tiles;
   p.m_tiles = pl.m_tiles;
   p.mode = pl.mode;
-  p.pair = pl.pair ? 1 : 0;
+  p.pair = pl.kernel;
   p.c = c;
   p.ldc = ldc;
-  if (pl.mode == dk::gemm::SPLIT) {
+  if (pl.ws_bytes > 0) {
     if (!workspace || workspace_bytes < pl.ws_bytes)
       return fail(DK_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", what, pl.ws_bytes,
                   workspace_bytes);
     if (!aligned16(workspace)) return fail(DK_ERR_WORKSPACE, "%s: workspace must be 16-byte aligned", what);
-    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.partials_off);
+    if (pl.mode == dk::gemm::SPLIT) p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.partials_off);
+    if (pl.stash) p.stash = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.stash_off);
   }
+  if (pl.kernel == 2 && pl.group == dk::gemm::kSlices && !p.stash)
+    return fail(DK_ERR_WORKSPACE, "%s: the wide schedule needs its stash", what);
   if (e.mode == DK_EPI_RESIDUAL_RMSNORM) {
     const NormSpec nm{e.norm_w, e.norm_w_dtype, e.norm_out, e.norm_ld, e.norm_eps};
     p.epi.mode = DK_EPI_RESIDUAL;   // the GEMM (or its fold) writes C; the norm follows from it
@@ -1355,11 +1430,16 @@ int dk_attention_batch_variant(const void* q, int64_t q_stride_b, int64_t q_stri
 size_t dk_attention_noalloc_scratch_limit(void) { return kNoAllocScratchBytes; }
 
 // Test hook, deliberately absent from the public header: which kernel runs invariant matmuls
-// (0 = the planner's choice, 1 = one-CTA kernel, 2 = CTA-pair kernel), so a test can compare the
-// two schedules' bits on the same shapes.  Returns the previous setting.
+// (low 4 bits: 0 = the planner's choice, 1 = one-CTA kernel, 2 = CTA-pair kernel, 3 = wide CTA-pair
+// kernel; bits 4 and up: slices per work unit, 0 = the planner's choice, else 1, 2, 4 or 8), so a
+// test can compare the schedules' bits on the same shapes.  Returns the previous setting.
 int dk_matmul_pair_schedule_for_test(int mode) {
-  const int prev = g_pair_override;
-  if (mode >= 0 && mode <= 2) g_pair_override = mode;
+  const int prev = g_pair_override | (g_group_override << 4);
+  const int kernel = mode & 15, group = mode >> 4;
+  if (kernel <= 3 && (group == 0 || group == 1 || group == 2 || group == 4 || group == 8)) {
+    g_pair_override = kernel;
+    g_group_override = group;
+  }
   return prev;
 }
 

@@ -1,7 +1,8 @@
-"""The CTA-pair GEMM (tcgen05.mma.cta_group::2, 256 weight columns x 128 tokens per
-pair) against the one-CTA GEMM: the same bits on the same shapes, for plain stores,
-split-K schedules and fused epilogues.  A test hook that is not part of the public
-header forces either kernel."""
+"""The CTA-pair GEMMs (tcgen05.mma.cta_group::2: 256 weight columns x 128 tokens per pair,
+and the wide kernel's 256 x 256) against the one-CTA GEMM: the same bits on the same shapes,
+for plain stores, every split-K schedule and fused epilogues.  A test hook that is not part
+of the public header forces the kernel (low 4 bits: 1 one-CTA, 2 pair, 3 wide) and the
+slices per work unit (bits 4 and up: 1, 2, 4 or 8; 0 = the planner's choice)."""
 import ctypes
 
 import pytest
@@ -26,8 +27,9 @@ def restore_schedule():
     _force(0)
 
 
+@pytest.mark.parametrize("kernel", [2, 3])
 @pytest.mark.parametrize("M,N,K", SHAPES)
-def test_pair_kernel_equals_one_cta_kernel(dev, restore_schedule, M, N, K):
+def test_pair_kernel_equals_one_cta_kernel(dev, restore_schedule, M, N, K, kernel):
     import torch
 
     from detkernels_b200.kernels.matmul import matmul_batch_invariant
@@ -36,7 +38,7 @@ def test_pair_kernel_equals_one_cta_kernel(dev, restore_schedule, M, N, K):
     b = (0.02 * torch.randn(K, N, device=dev, generator=g)).to(torch.bfloat16)
     _force(1)
     want = matmul_batch_invariant(a, b)
-    _force(2)
+    _force(kernel)
     got = matmul_batch_invariant(a, b)
     torch.cuda.synchronize()
     assert torch.equal(got, want)
@@ -44,12 +46,32 @@ def test_pair_kernel_equals_one_cta_kernel(dev, restore_schedule, M, N, K):
     a16, b16 = a.to(torch.float16), b.to(torch.float16)
     _force(1)
     want16 = matmul_batch_invariant(a16, b16)
-    _force(2)
+    _force(kernel)
     assert torch.equal(matmul_batch_invariant(a16, b16), want16)
 
 
-@pytest.mark.parametrize("epilogue", ["residual_rmsnorm", "silu_mul", "argmax", "silu"])
-def test_pair_kernel_fused_epilogues(dev, restore_schedule, epilogue):
+@pytest.mark.parametrize("group", [1, 2, 4, 8])
+@pytest.mark.parametrize("M,N,K", [(700, 1000, 4096), (257, 3072, 1024), (40, 512, 200)])
+def test_wide_kernel_every_group_equals_one_cta_kernel(dev, restore_schedule, M, N, K, group):
+    """Every slice grouping of the wide kernel (SPLIT launches for 1, 2 and 4 slices per unit, the
+    stash for 8) against the one-CTA kernel with the planner's grouping."""
+    import torch
+
+    from detkernels_b200.kernels.matmul import matmul_batch_invariant
+    g = torch.Generator(device=dev).manual_seed(M * 7 + N + K + group)
+    a = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    b = (0.02 * torch.randn(K, N, device=dev, generator=g)).to(torch.bfloat16)
+    _force(1)
+    want = matmul_batch_invariant(a, b)
+    _force(3 | (group << 4))
+    got = matmul_batch_invariant(a, b)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("kernel", [2, 3])
+@pytest.mark.parametrize("epilogue", ["residual_rmsnorm", "silu_mul", "argmax", "silu", "residual"])
+def test_pair_kernel_fused_epilogues(dev, restore_schedule, epilogue, kernel):
     import torch
 
     from detkernels_b200.kernels.matmul import matmul_fused
@@ -60,12 +82,14 @@ def test_pair_kernel_fused_epilogues(dev, restore_schedule, epilogue):
     r = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
     w = (1 + 0.1 * torch.randn(N, device=dev, generator=g)).to(torch.bfloat16)
     outs = []
-    for mode in (1, 2):
+    for mode in (1, kernel):
         _force(mode)
         if epilogue == "residual_rmsnorm":
             nrm = torch.empty_like(r)
             y = matmul_fused(a, b, "residual_rmsnorm", residual=r, norm_weight=w, norm_out=nrm)
             outs.append((y, nrm))
+        elif epilogue == "residual":
+            outs.append((matmul_fused(a, b, "residual", residual=r),))
         elif epilogue == "argmax":
             keys = torch.zeros(M, dtype=torch.int64, device=dev)
             matmul_fused(a, b, "argmax", argmax_keys=keys)
