@@ -349,9 +349,10 @@ GemmPlan plan_invariant(int64_t M, int64_t N, int64_t K, int sms) {
     end = pl.partials_off + sizeof(float) * static_cast<size_t>(dk::gemm::kSlices / group) * M * N;
   }
   if (pl.kernel == 2 && group == dk::gemm::kSlices) {
-    // one stash per CTA the launch can hold resident (at most one CTA per SM)
+    // one stash per CTA the launch can hold resident (at most one CTA per SM), after the
+    // workspace's arrival counters, which must stay zero for the other entry points
     pl.stash = true;
-    pl.stash_off = (end + 255) / 256 * 256;
+    pl.stash_off = ((end > kCounterBytes ? end : kCounterBytes) + 255) / 256 * 256;
     end = pl.stash_off + sizeof(float) * static_cast<size_t>(dk::gemm::kWideStashFloats) * sms;
   }
   pl.ws_bytes = end;

@@ -115,3 +115,21 @@ def test_pair_kernel_rows_equal_one_cta_rows_at_other_m(dev, restore_schedule):
     _force(1)
     for m in (1, 64, 256):
         assert torch.equal(matmul_batch_invariant(a[:m].contiguous(), b)[0], big[0]), m
+
+
+@pytest.mark.parametrize("group", [0, 1, 8])
+def test_wide_kernel_leaves_the_workspace_counters_zero(dev, restore_schedule, group):
+    """The workspace a stream shares between entry points starts with arrival counters that must
+    stay zero between calls; the wide kernel's stash and split partials live after them."""
+    import torch
+
+    from detkernels_b200 import _lib
+    from detkernels_b200.kernels.matmul import matmul_batch_invariant
+    g = torch.Generator(device=dev).manual_seed(77 + group)
+    a = torch.randn(1024, 2048, device=dev, generator=g).to(torch.bfloat16)
+    b = (0.02 * torch.randn(2048, 1536, device=dev, generator=g)).to(torch.bfloat16)
+    _force(3 | (group << 4))
+    matmul_batch_invariant(a, b)
+    torch.cuda.synchronize()
+    ws = _lib.workspace(1, a.device, _lib.stream_ptr(a.device))
+    assert int(ws[: 1 << 20].count_nonzero()) == 0      # DK_WORKSPACE_COUNTER_BYTES
