@@ -57,7 +57,9 @@ namespace gemm {
 
 constexpr int kTileN = 128;  // weight columns per tile (UMMA M)
 constexpr int kTileM = 128;  // tokens per tile (UMMA N)
-constexpr int kBK = 64;      // K per pipeline stage: one 128-byte swizzle row of bf16
+constexpr int kBK = 64;      // K per sub-block: one 128-byte swizzle row of bf16
+constexpr int kSub = 2;      // sub-blocks per pipeline stage of the one-CTA kernel
+constexpr int kStageK = kSub * kBK;   // K per pipeline stage (128): fewer barrier round trips per MMA
 constexpr int kUK = 16;      // K per tcgen05.mma, kind::f16
 constexpr int kMaxStages = 16;   // ring depth is chosen per launch from the stage size
 constexpr int kSlices = DK_MATMUL_K_SLICES;
@@ -78,14 +80,17 @@ constexpr int kSmemBytes = 232448;               // the sm_100 per-CTA maximum
 // kEpiStageBytes of the ring region, so FOLD launches run a shorter ring.
 constexpr int kRingBytes = kSmemBytes - 1024 /*align*/ - kBarrierBytes;
 
-// Stage size for an activation box of a_rows rows: 16 KB of weights + a_rows x 128 B,
-// rounded up to the 1 KB swizzle period.  The MMA always reads 128 token rows
-// (16 KB) from a stage's activation region, i.e. up to (128 - a_rows) x 128 B
-// past the loaded rows: into the next stage (stale data, feeding columns that
-// are never stored) and, after the last stage, into a guard area kept free at
-// the end of the ring so that every read stays inside the CTA's shared memory.
+// Stage layout for an activation box of a_rows rows (a multiple of 8):
+//   [weights sub-block 0 | weights sub-block 1 | tokens sub-block 0 | tokens sub-block 1]
+// with 16 KB per weight sub-block (128 columns x 64 k) and a_rows x 128 B per token
+// sub-block (each a multiple of the 1 KB swizzle period), the whole rounded up to 1 KB.
+// The MMA always reads 128 token rows (16 KB) from a token sub-block, i.e. up to
+// (128 - a_rows) x 128 B past its loaded rows: into the next sub-block or stage (stale
+// data, feeding columns that are never stored) and, after the last stage, into a guard
+// area kept free at the end of the ring so that every read stays inside the CTA's
+// shared memory.
 __host__ __device__ __forceinline__ int stage_bytes_for(int a_rows) {
-  return ((kWTileBytes + a_rows * kBK * 2 + 1023) / 1024) * 1024;
+  return ((kSub * (kWTileBytes + a_rows * kBK * 2) + 1023) / 1024) * 1024;
 }
 __host__ __device__ __forceinline__ int overhang_bytes_for(int a_rows) { return (kTileM - a_rows) * kBK * 2; }
 __host__ __device__ __forceinline__ int ring_bytes_for(int mode) {
@@ -532,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int fills = 0;                     // stage fills issued so far (round robin)
-      const uint32_t tx_bytes = kWTileBytes + p.a_rows * kBK * 2;
+      const uint32_t tx_bytes = kSub * (kWTileBytes + p.a_rows * kBK * 2);
       for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x) {
         const int g = u % n_groups;
         const int t = u / n_groups;
@@ -542,16 +547,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = p.slice_begin + g * p.group + si;
           int k0, k1;
           slice_bounds(p, s, k0, k1);
-          const int nkb = (k1 - k0 + kBK - 1) / kBK;
+          const int nkb = (k1 - k0 + kStageK - 1) / kStageK;
           for (int kb = 0; kb < nkb; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, kDetProdEmpty, abort_flag)) break;
             uint8_t* st = smem + stage * stage_bytes;
             mbar_arrive_expect_tx(&full[stage], tx_bytes);
-            const int kk = k0 + kb * kBK;
-            const int kl = kk - p.k_base;   // coordinate inside the K range held in memory
-            tma_load_2d(st, &tmB, &full[stage], nt * kTileN, kl);
-            tma_load_2d(st + kWBoxBytes, &tmB, &full[stage], nt * kTileN + 64, kl);
-            tma_load_2d(st + kWTileBytes, &tmA, &full[stage], kl, mt * kTileM);
+            // both sub-blocks are always loaded (past the slice's end their MMAs are not issued;
+            // past the K range held in memory the copy reads zeros), so the byte count is fixed
+#pragma unroll
+            for (int sb = 0; sb < kSub; ++sb) {
+              const int kl = k0 + kb * kStageK + sb * kBK - p.k_base;   // inside the K range in memory
+              uint8_t* wst = st + sb * kWTileBytes;
+              tma_load_2d(wst, &tmB, &full[stage], nt * kTileN, kl);
+              tma_load_2d(wst + kWBoxBytes, &tmB, &full[stage], nt * kTileN + 64, kl);
+              tma_load_2d(st + kSub * kWTileBytes + sb * p.a_rows * kBK * 2, &tmA, &full[stage], kl, mt * kTileM);
+            }
             ++fills;
             if (++stage == n_stages) {
               stage = 0;
@@ -581,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = p.slice_begin + g * p.group + si;
           int k0, k1;
           slice_bounds(p, s, k0, k1);
-          const int nkb = (k1 - k0 + kBK - 1) / kBK;
+          const int nkb = (k1 - k0 + kStageK - 1) / kStageK;
           const int slot = slot_of(si, ordinal, p.group);
           // the slot's previous value must have been released by the epilogue
           if (!mbar_wait(&slot_free[slot], ((use_par >> slot) & 1u) ^ 1u, kDetMmaSlotFree, abort_flag)) break;
@@ -591,16 +601,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kb = 0; kb < nkb; ++kb) {
             if (!mbar_wait(&full[stage], phase, kDetMmaFull, abort_flag)) break;
             tc_fence_after();
-            const int kk = k0 + kb * kBK;
-            const int nsteps = min(kBK / kUK, (k1 - kk + kUK - 1) / kUK);
+            const int kk = k0 + kb * kStageK;
+            const int nsteps = min(kStageK / kUK, (k1 - kk + kUK - 1) / kUK);
             const uint32_t b_base = smem_u32(smem + stage * stage_bytes);
-            const uint32_t a_base = b_base + kWTileBytes;
+            const uint32_t a_base = b_base + kSub * kWTileBytes;
             for (int j = 0; j < nsteps; ++j) {
+              const int sb = j >> 2, jj = j & 3;   // sub-block, 16-deep step inside it
               // B (weights) MN-major, 128B swizzle: 64-column groups 8 KB apart (LBO),
               // 8-row K groups 1 KB apart (SBO); one 16-deep K step = 2 KB.
-              const uint64_t bdesc = umma_sdesc(b_base + j * 2048, kWBoxBytes, 1024, 2);
+              const uint64_t bdesc = umma_sdesc(b_base + sb * kWTileBytes + jj * 2048, kWBoxBytes, 1024, 2);
               // A (tokens) K-major, 128B swizzle: 8-row groups 1 KB apart; 16 K = 32 bytes.
-              const uint64_t adesc = umma_sdesc(a_base + j * 32, 16, 1024, 2);
+              const uint64_t adesc = umma_sdesc(a_base + sb * (p.a_rows * kBK * 2) + jj * 32, 16, 1024, 2);
               tc_mma_f16(d_tmem, bdesc, adesc, idesc, (kb > 0 || j > 0) ? 1u : 0u);
             }
             tc_commit(&empty[stage]);
@@ -706,9 +717,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!last) tmem_st_wait();
         tc_fence_before();
         // release every slot consumed here; the result slot stays unless this was the unit's end
-        if (nlev > 0) mbar_arrive(&slot_free[slot]);
-        for (int l = 0; l + 1 < nlev; ++l) mbar_arrive(&slot_free[(stack >> (2 * l)) & 3u]);
-        if (last) mbar_arrive(&slot_free[res_slot]);
+        if (nlev > 0) mbar_arrive_relaxed(&slot_free[slot]);
+        for (int l = 0; l + 1 < nlev; ++l) mbar_arrive_relaxed(&slot_free[(stack >> (2 * l)) & 3u]);
+        if (last) mbar_arrive_relaxed(&slot_free[res_slot]);
         if (!last) stack = (stack & ~(3u << (2 * nlev))) | (static_cast<uint32_t>(res_slot) << (2 * nlev));
       }
       if (abort_flag) break;

@@ -12,10 +12,16 @@
 // the one-CTA 128 x 128 tile.  TMA delivery into shared memory (about 55-70 bytes per cycle
 // per SM with every SM streaming) is what bounds the smaller tile.
 //
-// Accumulators: one slice partial of the CTA's 128 columns x 256 tokens takes 256 TMEM
+// Operand roles: the 256 tokens of a pair tile are the instruction's M (each CTA's 128 token
+// rows are its TMEM lanes) and the 256 weight columns its N, so an epilogue thread owns one
+// token row of consecutive output columns and stores it without a transpose.  (The one-CTA
+// kernel puts weights on M instead, so that a few decode tokens still fill the instruction;
+// which operand is A does not change an output element's bits.)
+//
+// Accumulators: one slice partial of the CTA's 128 tokens x 256 columns takes 256 TMEM
 // columns, so TMEM holds two (slots X and Y, used alternately).  The tree needs up to four
 // live values, so the pending left operands live elsewhere:
-//   * R: the epilogue threads' registers (thread = one TMEM lane x 128 token columns,
+//   * R: the epilogue threads' registers (thread = one TMEM lane x 128 weight columns,
 //     128 f32 registers), holding p0 / p0+p1 (and p4 / p4+p5);
 //   * p2 (p6) stays in its slot until p3 (p7) arrives;
 //   * S: the 8-slice unit's left half (p0+p1)+(p2+p3), parked in a global stash (L2) while
@@ -57,8 +63,7 @@ constexpr int kWideThreads = 128 + 32 * kWideEpiWarps; // 384
 constexpr int kWideEpiCols = kWideTileM / 2;           // token columns per epilogue thread (128)
 constexpr int kWideChunks = kWideEpiCols / 32;         // 4 chunks of 32 columns
 constexpr int kWideEpiArrivals = 2 * kWideEpiWarps;    // slot_free arrivals: epilogue warps of both CTAs
-constexpr int kWideEpiStageBytes = kWideEpiWarps * 32 * kStagePitch * 4;
-constexpr int kWideRingBytes = kSmemBytes - 1024 - kBarrierBytes - kWideEpiStageBytes;
+constexpr int kWideRingBytes = kSmemBytes - 1024 - kBarrierBytes;
 constexpr int kWideStages = kWideRingBytes / kWideStageBytes;   // 3 (6 of one sub-block)
 constexpr int kWideLaunchRegs = 168;                   // 65536 / 384, rounded down to 8
 constexpr int kWideProducerRegs = 56;
@@ -77,6 +82,11 @@ __device__ __forceinline__ void tc_commit_both(const uint64_t* bar) {
           smem_u32(bar)),
       "h"(static_cast<uint16_t>(3))
       : "memory");
+}
+
+// Arrive (relaxed) on the mbarrier at cluster shared-memory address `addr`.
+__device__ __forceinline__ void mbar_arrive_relaxed_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
 }
 
 template <uint32_t N>
@@ -105,49 +115,84 @@ __device__ __forceinline__ void wide_ld(uint32_t lane_base, int slot, int c, boo
   }
 }
 
-// Final values (or, for SPLIT / PARTIAL, this unit's subtree sum) of chunk c -> memory.
+// Final values (or, for SPLIT / PARTIAL, this unit's subtree sum) of one token row m, columns
+// n_base .. n_base + 31 -> memory.  The thread owns the row, so no transpose is needed.  ARGMAX
+// only folds the chunk into the thread's running key (one atomic per row per unit, after the
+// last chunk).
 template <typename T, bool FOLDK>
-__device__ __forceinline__ void wide_emit(const Params& q, float* ws, T* C, float* stage, int n_first, int quarter,
-                                          int n, bool n_ok, int m0, int c, const float (&v)[32]) {
+__device__ __forceinline__ void wide_emit(const Params& q, float* ws, T* C, int m, int n_base, const float (&v)[32],
+                                          unsigned long long& best) {
+  const int ncols = min(32, q.N - n_base);
+  if (m >= q.M || ncols <= 0) return;
   if constexpr (FOLDK) {
-    (void)ws;
-    emit_rows<T>(q, C, stage, q.mode, n_first + quarter * 32, m0 + c * 32, v);
-  } else {
-    // SPLIT (ws already offset to this unit's group) or PARTIAL: the f32 subtree sum;
-    // consecutive lanes write consecutive columns (128-byte warp stores)
-    (void)C;
-    if (!n_ok) return;
+    if (q.epi.mode == DK_EPI_ARGMAX) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int m = m0 + c * 32 + j;
-      if (m < q.M) ws[static_cast<int64_t>(m) * q.N + n] = v[j];
+      for (int k = 0; k < 32; ++k) {
+        if (k < ncols) {
+          const unsigned long long key = argmax_key<T>(v[k], n_base + k);
+          best = key > best ? key : best;
+        }
+      }
+      if (C) {
+        float w[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) w[k] = v[k];
+        T* dst = C + static_cast<int64_t>(m) * q.ldc + n_base;
+        if (ncols == 32 && aligned_row<T>(C, q.ldc, n_base)) {
+          store_row_vec<T>(dst, w, 32);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            if (k < ncols) dst[k] = from_f32<T>(w[k]);
+        }
+      }
+      return;
+    }
+    float w[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) w[k] = v[k];
+    store_final_row<T>(q, C, m, n_base, ncols, w);
+  } else {
+    // SPLIT (ws already offset to this unit's group) or PARTIAL: the f32 subtree sum
+    (void)C;
+    (void)best;
+    float* dst = ws + static_cast<int64_t>(m) * q.N + n_base;
+    if (ncols == 32 && (q.N % 4) == 0) {
+#pragma unroll
+      for (int k = 0; k < 32; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        if (k < ncols) dst[k] = v[k];
     }
   }
 }
 
 // The epilogue warpgroups (warps 4..11).  Warp w reads TMEM lane quarter w % 4; the two warps
-// of a quarter split the 256 token columns into halves.  Thread <-> TMEM lane <-> weight column.
+// of a quarter split the 256 weight columns into halves.  Thread <-> TMEM lane <-> token row.
 template <typename T, bool FOLDK>
-__device__ __forceinline__ void wide_epilogue(const Params& p, uint8_t* smem, uint64_t* slot_full,
-                                              uint64_t* slot_free, uint32_t tmem_base, int units, int n_groups,
-                                              int pair, int n_pairs, uint32_t rank) {
+__device__ __forceinline__ void wide_epilogue(const Params& p, uint64_t* slot_full, uint64_t* slot_free,
+                                              uint32_t tmem_base, int units, int n_groups, int pair, int n_pairs,
+                                              uint32_t rank) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int ew = warp - 4;
   const int quarter = warp & 3;
   const int half = ew >> 2;
-  const int n_local = quarter * 32 + lane;
+  const int m_local = static_cast<int>(rank) * kWideRows + quarter * 32 + lane;   // token row in the pair tile
   const int col0 = half * kWideEpiCols;
   T* C = reinterpret_cast<T*>(p.c);
-  float* stage = reinterpret_cast<float*>(smem + kWideRingBytes) + ew * (32 * kStagePitch);
   const int64_t MN = static_cast<int64_t>(p.M) * p.N;
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(col0);
-  // this thread's 128 stash floats: [half][chunk][j][lane of the CTA's 128 columns]
-  float* stash = p.stash + static_cast<int64_t>(blockIdx.x) * kWideStashFloats + half * (kWideChunks * 32 * 128) +
-                 n_local;
+  // this thread's 128 stash floats as 32 float4: [half][chunk][quad][lane of the CTA's 128 rows],
+  // so a warp's 16-byte accesses cover 512 contiguous bytes
+  float4* stash = reinterpret_cast<float4*>(p.stash + static_cast<int64_t>(blockIdx.x) * kWideStashFloats) +
+                  half * (kWideChunks * 8 * 128) + quarter * 32 + lane;
   auto release = [&](int s) {
     __syncwarp();
-    if (lane == 0) mbar_arrive_cluster(cluster_addr(&slot_free[s], 0));
+    // relaxed: the TMEM reads are complete (tcgen05.wait::ld); release semantics would also wait
+    // for this thread's global stores, which the MMA issuer does not depend on
+    if (lane == 0) mbar_arrive_relaxed_cluster(cluster_addr(&slot_free[s], 0));
   };
   bool abort_flag = false;
   uint32_t cnt = 0;
@@ -156,10 +201,8 @@ __device__ __forceinline__ void wide_epilogue(const Params& p, uint8_t* smem, ui
   for (int u = pair; u < units && !abort_flag; u += n_pairs) {
     int g, mt, nt;
     wide_unit(p, u, n_groups, g, mt, nt);
-    const int n_first = nt * kWideTileN + static_cast<int>(rank) * kTileN;
-    const int n = n_first + n_local;
-    const int m0 = mt * kWideTileM + col0;
-    const bool n_ok = n < p.N;
+    const int m = mt * kWideTileM + m_local;
+    const int n0 = nt * kWideTileN + col0;
     float* ws = (p.mode == SPLIT) ? p.ws + static_cast<int64_t>(g) * MN : p.ws;
     int prev_slot = 0;
     bool prev_empty = false;
@@ -218,21 +261,32 @@ __device__ __forceinline__ void wide_epilogue(const Params& p, uint8_t* smem, ui
 #pragma unroll
           for (int c = 0; c < kWideChunks; ++c)
 #pragma unroll
-            for (int j = 0; j < 32; ++j) __stcg(stash + (c * 32 + j) * 128, R[c][j]);
+            for (int j = 0; j < 8; ++j)
+              __stcg(stash + (c * 8 + j) * 128, make_float4(R[c][4 * j], R[c][4 * j + 1], R[c][4 * j + 2], R[c][4 * j + 3]));
         }
       }
       if (si + 1 == p.group) {
+        unsigned long long best = 0ull;
         if (p.group == 8) {
 #pragma unroll
           for (int c = 0; c < kWideChunks; ++c) {
             float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(__ldcg(stash + (c * 32 + j) * 128), R[c][j]);
-            wide_emit<T, FOLDK>(p, ws, C, stage, n_first, quarter, n, n_ok, m0, c, v);
+            for (int j = 0; j < 8; ++j) {
+              const float4 s4 = __ldcg(stash + (c * 8 + j) * 128);
+              v[4 * j] = __fadd_rn(s4.x, R[c][4 * j]);
+              v[4 * j + 1] = __fadd_rn(s4.y, R[c][4 * j + 1]);
+              v[4 * j + 2] = __fadd_rn(s4.z, R[c][4 * j + 2]);
+              v[4 * j + 3] = __fadd_rn(s4.w, R[c][4 * j + 3]);
+            }
+            wide_emit<T, FOLDK>(p, ws, C, m, n0 + c * 32, v, best);
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < kWideChunks; ++c) wide_emit<T, FOLDK>(p, ws, C, stage, n_first, quarter, n, n_ok, m0, c, R[c]);
+          for (int c = 0; c < kWideChunks; ++c) wide_emit<T, FOLDK>(p, ws, C, m, n0 + c * 32, R[c], best);
+        }
+        if constexpr (FOLDK) {
+          if (p.epi.mode == DK_EPI_ARGMAX && best != 0ull) atomicMax(p.epi.argmax_keys + m, best);
         }
       }
     }
@@ -246,7 +300,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
     gemm_wide_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kWideRingBytes + kWideEpiStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kWideRingBytes);
   uint64_t* empty = full + kWideStages;
   uint64_t* slot_full = empty + kWideStages;
   uint64_t* slot_free = slot_full + kWideSlots;
@@ -349,7 +403,9 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t cnt = 0;   // slice partials issued; slot = cnt & 1
-      constexpr uint32_t idesc = umma_idesc_f16(FMT, /*a_mn=*/1, /*b_mn=*/0, kWideTileN, kWideTileM);
+      // A = tokens (K-major, 128 rows in each CTA: UMMA M = 256 tokens, TMEM lanes), B = weights
+      // (MN-major, 128 columns in each CTA: UMMA N = 256 columns)
+      constexpr uint32_t idesc = umma_idesc_f16(FMT, /*a_mn=*/0, /*b_mn=*/1, kWideTileM, kWideTileN);
       for (int u = pair; u < units && !abort_flag; u += n_pairs) {
         const int g = u % n_groups;
         for (int si = 0; si < p.group && !abort_flag; ++si) {
@@ -376,7 +432,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
               const int sb = j >> 2, jj = j & 3;
               const uint64_t bdesc = umma_sdesc(b_base + sb * kWTileBytes + jj * 2048, kWBoxBytes, 1024, 2);
               const uint64_t adesc = umma_sdesc(a_base + sb * (kWideRows * kBK * 2) + jj * 32, 16, 1024, 2);
-              tc_mma_f16_pair(d_tmem, bdesc, adesc, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+              tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || j > 0) ? 1u : 0u);
             }
             tc_commit_both(&empty[stage]);
             if (++stage == kWideStages) {
@@ -394,7 +450,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
     }
   } else {
     regs_inc<kWideEpiRegs>();
-    wide_epilogue<T, FOLDK>(p, smem, slot_full, slot_free, tmem_base, units, n_groups, pair, n_pairs, rank);
+    wide_epilogue<T, FOLDK>(p, slot_full, slot_free, tmem_base, units, n_groups, pair, n_pairs, rank);
   }
 
   __syncwarp();

@@ -296,7 +296,9 @@ int pick_group(int64_t M, int64_t N, int64_t K, int64_t tiles, int sms, int kern
                                           : dk::gemm::stage_bytes_for(a_rows);
   const double kSmBytesPerUs = 100e3;   // sustained TMA bytes per SM per microsecond
   const double kL2BytesPerUs = 10e6;    // L2 bytes per microsecond for the partial round trip
-  const int64_t kb_per_slice = ceil_div(slice_len_for(K, dk::gemm::kSlices), dk::gemm::kBK);
+  const int64_t kb_per_slice = ceil_div(slice_len_for(K, dk::gemm::kSlices), kernel == 2   ? dk::gemm::kWideBK
+                                                                      : kernel == 1 ? dk::gemm::kBK
+                                                                                    : dk::gemm::kStageK);
   double best = 1e30;
   int best_g = dk::gemm::kSlices;
   for (int g = dk::gemm::kSlices; g >= 1; g /= 2) {
@@ -323,17 +325,23 @@ int g_pair_override = 0;
 // of 32 KB, but measured on B200 it is not faster than the one-CTA kernel (M = 2048, N = 4096:
 // 147 vs 129 us); it runs only when forced.  The wide kernel (256 x 256 tiles, 16 KB per SM per
 // 128 x 128 x 64) runs when the token count fills its 256-token tiles.
-int pick_kernel(int64_t M, int64_t N) {
-  (void)N;
+int pick_kernel(int64_t M, int64_t N, int64_t K, int sms) {
   if (g_pair_override == 1) return 0;
   if (g_pair_override == 2) return 1;
   if (g_pair_override == 3) return 2;
-  return (M > dk::gemm::kTileM) ? 2 : 0;
+  // Measured on B200 (CUDA graph, weights beyond L2): above 256 tokens the wide kernel wins; at
+  // 129-256 tokens only when there are a wave of 256-column tiles for its 8-slice units (the LM
+  // head, N = 32000: 47 vs 61 us); with fewer tiles it needs split-K partials, whose row-wise
+  // stores make it slower than the one-CTA kernel (N = 11008, K = 4096: 64 vs 50 us).
+  (void)K;
+  if (M > 2 * dk::gemm::kTileM) return 2;
+  if (M > dk::gemm::kTileM && ceil_div(N, dk::gemm::kWideTileN) >= sms / 2) return 2;
+  return 0;
 }
 
 GemmPlan plan_invariant(int64_t M, int64_t N, int64_t K, int sms) {
   GemmPlan pl{};
-  pl.kernel = pick_kernel(M, N);
+  pl.kernel = pick_kernel(M, N, K, sms);
   const int tile_n = pl.kernel ? dk::gemm::kPairTileN : dk::gemm::kTileN;
   const int tile_m = (pl.kernel == 2) ? dk::gemm::kWideTileM : dk::gemm::kTileM;
   pl.n_tiles = static_cast<int>(ceil_div(N, tile_n));
