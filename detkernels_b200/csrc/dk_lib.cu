@@ -142,35 +142,16 @@ int encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* b
 bool valid_dtype(int d) { return d == DK_F32 || d == DK_F16 || d == DK_BF16; }
 
 // ============================ RMSNorm ============================
-// Streaming vector RMSNorm over `rows` rows of at most MAXC * 256 chunks (<= 16 KB): as many
-// CTAs as fit on the GPU at once (never more than rows), each walking rows b, b + grid, ... with
-// kRmsRing rows in flight in a shared-memory ring.
+// Streaming vector RMSNorm over `rows` rows of at most MAXC * 256 chunks (<= 16 KB): a persistent
+// grid of kRmsStreamPerSm CTAs per SM (never more than rows), each walking rows b, b + grid, ...
+// with the next row's chunks in flight in registers.
 template <typename T, typename W, int MAXC>
-cudaError_t rmsnorm_ring(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int64_t cols,
-                         float eps, cudaStream_t st) {
-  static int per_sm[kMaxDevices] = {};
-  static bool smem_set[kMaxDevices] = {};
-  const int dev = current_device();
-  auto fn = dk::rmsnorm_inv_ring_kernel<T, W, MAXC>;
-  const int smem = dk::kRmsRing * static_cast<int>((cols * sizeof(T) + 127) / 128 * 128);
-  if (dev >= 0 && dev < kMaxDevices && !smem_set[dev]) {
-    const int max_smem = dk::kRmsRing * MAXC * dk::kRmsThreads * 16;
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-    if (e != cudaSuccess) return e;
-    smem_set[dev] = true;
-  }
-  int blocks = (dev >= 0 && dev < kMaxDevices) ? per_sm[dev] : 0;
-  if (blocks <= 0) {
-    const int max_smem = dk::kRmsRing * MAXC * dk::kRmsThreads * 16;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, dk::kRmsThreads, max_smem) != cudaSuccess ||
-        blocks <= 0)
-      blocks = 1;
-    if (dev >= 0 && dev < kMaxDevices) per_sm[dev] = blocks;
-  }
-  const int64_t cap = static_cast<int64_t>(blocks) * sm_count(dev);
+cudaError_t rmsnorm_stream(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int64_t cols,
+                           float eps, cudaStream_t st) {
+  const int64_t cap = static_cast<int64_t>(dk::kRmsStreamPerSm) * sm_count(current_device());
   const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
-  return launch_pdl(fn, dim3(grid), dim3(dk::kRmsThreads), smem, st, static_cast<const T*>(x), xs,
-                    static_cast<const W*>(w), static_cast<T*>(y), ys, rows, cols, eps);
+  return launch_pdl(dk::rmsnorm_inv_stream_kernel<T, W, MAXC>, dim3(grid), dim3(dk::kRmsThreads), 0, st,
+                    static_cast<const T*>(x), xs, static_cast<const W*>(w), static_cast<T*>(y), ys, rows, cols, eps);
 }
 
 template <typename T, typename W>
@@ -182,10 +163,9 @@ int rmsnorm_inv_launch(const void* x, int64_t xs, const void* w, void* y, int64_
   const int64_t per_thread = (cols / VEC + dk::kRmsThreads - 1) / dk::kRmsThreads;   // chunks per thread
   cudaError_t e;
   if (vec && rows > 1 && per_thread >= 3 && per_thread <= 4) {
-    // rows of 3-4 chunks per thread (12-16 KB: 4096 f32, 8192 16-bit elements): streamed through
-    // a shared-memory ring by persistent CTAs.  Shorter rows keep one CTA per row (measured: a
-    // persistent CTA's per-row barriers then dominate).
-    e = rmsnorm_ring<T, W, 4>(x, xs, w, y, ys, rows, cols, eps, st);
+    // rows of 3-4 chunks per thread (12-16 KB: 4096 f32, 8192 16-bit elements): streamed by
+    // persistent CTAs that hold the next row in registers.  Shorter rows keep one CTA per row.
+    e = rmsnorm_stream<T, W, 4>(x, xs, w, y, ys, rows, cols, eps, st);
   } else if (vec) {
     constexpr int MAXC = (sizeof(T) == 4) ? 8 : 4;
     e = launch_pdl(dk::rmsnorm_inv_vec_kernel<T, W, MAXC>, grid, dim3(dk::kRmsThreads), 0, st,
