@@ -21,6 +21,7 @@
 #include "dk_attention_variant.cuh"
 #include "dk_gdn.cuh"
 #include "dk_gdn_tc.cuh"
+#include "dk_gdn_umma.cuh"
 
 namespace {
 
@@ -686,10 +687,41 @@ int gdn_launch_tc(const dk::gdn::Params& p, int64_t n_seqs, cudaStream_t st) {
   return DK_OK;
 }
 
+// Which kernel runs chunked bf16 GDN with head dim 128: 0 = the tcgen05 kernel, 1 = the mma.sync
+// kernel.  Only the test hook dk_gdn_kernel_for_test sets it.
+int g_gdn_override = 0;
+
+// Chunked bf16, head dim 128, on tcgen05 (gdn_chunk_umma_kernel): K, Q and V chunks by TMA through
+// 2-D maps over the packed [tokens, heads x 128] tensors.
+int gdn_launch_umma(const dk::gdn::Params& p, int64_t n_seqs, cudaStream_t st) {
+  static bool done[kMaxDevices] = {};
+  auto fn = dk::gdn::gdn_chunk_umma_kernel;
+  int rc = ensure_smem(fn, dk::gdn::kUmSmem, done);
+  if (rc) return rc;
+  const int64_t rows = p.cu_seqlens ? p.seq_len : n_seqs * p.seq_len;
+  if (rows <= 0) return DK_OK;
+  if (rows > 0x7fffffffLL) return fail(DK_ERR_UNSUPPORTED, "gdn: more than 2^31 tokens");
+  CUtensorMap tk, tq, tv;
+  const uint64_t dqk[2] = {static_cast<uint64_t>(p.H) * dk::gdn::kUmD, static_cast<uint64_t>(rows)};
+  const uint64_t sqk[1] = {static_cast<uint64_t>(p.H) * dk::gdn::kUmD * 2};
+  const uint64_t dvv[2] = {static_cast<uint64_t>(p.HV) * dk::gdn::kUmD, static_cast<uint64_t>(rows)};
+  const uint64_t svv[1] = {static_cast<uint64_t>(p.HV) * dk::gdn::kUmD * 2};
+  const uint32_t box[2] = {64, static_cast<uint32_t>(dk::gdn::kChunk)};
+  const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if ((rc = encode_map(&tk, dt, 2, p.k, dqk, sqk, box, CU_TENSOR_MAP_SWIZZLE_128B, "gdn"))) return rc;
+  if ((rc = encode_map(&tq, dt, 2, p.q, dqk, sqk, box, CU_TENSOR_MAP_SWIZZLE_128B, "gdn"))) return rc;
+  if ((rc = encode_map(&tv, dt, 2, p.v, dvv, svv, box, CU_TENSOR_MAP_SWIZZLE_128B, "gdn"))) return rc;
+  cudaError_t e = launch_pdl(fn, dim3(p.HV, static_cast<unsigned>(n_seqs)), dim3(dk::gdn::kUmThreads),
+                             dk::gdn::kUmSmem, st, tk, tq, tv, p);
+  if (e != cudaSuccess) return fail(DK_ERR_CUDA, "gdn: launch failed: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
+
 template <typename T>
 int gdn_launch_dims(const dk::gdn::Params& p, int dk_, int dv_, int64_t n_seqs, cudaStream_t st) {
-  // chunked bf16 with head dims 64/128: tensor-core kernel; otherwise the f32 CUDA-core kernel
+  // chunked bf16: head dim 128 on tcgen05, 64 on mma.sync; otherwise the f32 CUDA-core kernel
   if (std::is_same<T, __nv_bfloat16>::value && p.chunk == dk::gdn::kChunk && dk_ == dv_) {
+    if (dk_ == 128 && g_gdn_override == 0) return gdn_launch_umma(p, n_seqs, st);
     if (dk_ == 128) return gdn_launch_tc<128>(p, n_seqs, st);
     if (dk_ == 64) return gdn_launch_tc<64>(p, n_seqs, st);
   }
@@ -1429,6 +1461,14 @@ int dk_matmul_pair_schedule_for_test(int mode) {
     g_pair_override = kernel;
     g_group_override = group;
   }
+  return prev;
+}
+
+// Test hook, deliberately absent from the public header: which kernel runs chunked bf16 GDN with
+// head dim 128 (0 = the tcgen05 kernel, 1 = the mma.sync kernel).  Returns the previous setting.
+int dk_gdn_kernel_for_test(int mode) {
+  const int prev = g_gdn_override;
+  if (mode == 0 || mode == 1) g_gdn_override = mode;
   return prev;
 }
 

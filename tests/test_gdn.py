@@ -65,11 +65,12 @@ def test_matches_fla_naive_golden_fixture(dev):
     np.testing.assert_allclose(_np(final), d["final"], rtol=S_RTOL, atol=S_ATOL)
 
 
-def test_rectangular_batch_equals_packed_bitwise(dev):
+@pytest.mark.parametrize("D", [64, 128])
+def test_rectangular_batch_equals_packed_bitwise(dev, D):
     """The same sequences as B rows of length T or packed with cu_seqlens: same bits."""
     import torch
     from detkernels_b200.kernels.gdn import chunk_gated_delta_rule
-    q, k, v, gate, beta, cu, s0 = _inputs(dev, [100] * 3, 2, 4, 64, torch.bfloat16, seed=5, h0=True)
+    q, k, v, gate, beta, cu, s0 = _inputs(dev, [100] * 3, 2, 4, D, torch.bfloat16, seed=5, h0=True)
     o_p, f_p = chunk_gated_delta_rule(q, k, v, gate, beta, initial_state=s0, output_final_state=True, cu_seqlens=cu)
     r = [x.view(3, 100, *x.shape[2:]) for x in (q, k, v, gate, beta)]
     o_r, f_r = chunk_gated_delta_rule(*r[:3], r[3], r[4], initial_state=s0, output_final_state=True)
@@ -82,6 +83,49 @@ def test_zero_length_sequences_pass_the_state_through(dev):
     q, k, v, gate, beta, cu, s0 = _inputs(dev, [0, 9, 0], 2, 2, 32, torch.bfloat16, seed=6, h0=True)
     o, final = chunk_gated_delta_rule(q, k, v, gate, beta, initial_state=s0, output_final_state=True, cu_seqlens=cu)
     assert torch.equal(final[0], s0[0].float()) and torch.equal(final[2], s0[2].float())
+
+
+def test_pack_position_does_not_change_a_sequences_bits_d128(dev):
+    """A 200-token sequence alone, first in a pack and last in a pack of ragged neighbours (whose
+    tokens sit right after / before it in memory): the same output and state bits."""
+    import torch
+    from detkernels_b200.kernels.gdn import chunk_gated_delta_rule
+    q, k, v, gate, beta, cu, s0 = _inputs(dev, [37, 200, 131], 2, 4, 128, torch.bfloat16, seed=11, h0=True)
+    o, f = chunk_gated_delta_rule(q, k, v, gate, beta, initial_state=s0, output_final_state=True, cu_seqlens=cu)
+    sl = slice(37, 237)
+    alone = [x[:, sl].contiguous() for x in (q, k, v, gate, beta)]
+    o1, f1 = chunk_gated_delta_rule(*alone, initial_state=s0[1:2], output_final_state=True,
+                                    cu_seqlens=torch.tensor([0, 200], device=dev))
+    assert torch.equal(o1[0], o[0, sl]) and torch.equal(f1[0], f[1])
+    # the same sequence moved to the front of another pack
+    perm = [x[:, list(range(37, 237)) + list(range(0, 37))].contiguous() for x in (q, k, v, gate, beta)]
+    o2, f2 = chunk_gated_delta_rule(*perm, initial_state=torch.stack([s0[1], s0[0]]), output_final_state=True,
+                                    cu_seqlens=torch.tensor([0, 200, 237], device=dev))
+    assert torch.equal(o2[0, :200], o[0, sl]) and torch.equal(f2[0], f[1])
+
+
+def test_tcgen05_and_mma_sync_chunk_kernels_agree(dev):
+    """The tcgen05 chunk kernel (head dim 128) against the mma.sync one it replaced, both within the
+    oracle tolerance of each other (their f32 sums run in different orders)."""
+    import ctypes
+
+    import torch
+
+    from detkernels_b200 import _lib
+    from detkernels_b200.kernels.gdn import chunk_gated_delta_rule
+    hook = _lib.load().dk_gdn_kernel_for_test   # a test hook outside the public header
+    hook.restype, hook.argtypes = ctypes.c_int, [ctypes.c_int]
+    q, k, v, gate, beta, cu, s0 = _inputs(dev, [1, 64, 65, 700, 2000], 4, 8, 128, torch.bfloat16, seed=12, h0=True)
+    try:
+        hook(1)
+        o_old, f_old = chunk_gated_delta_rule(q, k, v, gate, beta, initial_state=s0, output_final_state=True,
+                                              cu_seqlens=cu)
+    finally:
+        hook(0)
+    o_new, f_new = chunk_gated_delta_rule(q, k, v, gate, beta, initial_state=s0, output_final_state=True,
+                                          cu_seqlens=cu)
+    torch.testing.assert_close(o_new.float(), o_old.float(), rtol=O_RTOL, atol=O_ATOL)
+    torch.testing.assert_close(f_new, f_old, rtol=S_RTOL, atol=S_ATOL)
 
 
 def test_chunked_and_recurrent_agree(dev):
