@@ -123,6 +123,14 @@ __device__ __forceinline__ uint64_t mnmaj(uint32_t saddr, uint32_t group_bytes) 
   return umma_sdesc(saddr, group_bytes, 1024, 2);
 }
 
+// exp(x) for x <= 0 as 2^(x log2 e) by the single hardware instruction (relative error ~2^-22);
+// used for the decay factors exp(gamma_t - gamma_j) of the chunk's 64 x 64 matrices.
+__device__ __forceinline__ float um_exp_nonpos(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmul_rn(x, 1.44269504088896341f)));
+  return y;
+}
+
 enum : int {
   kDetUmLoad = 0x540,
   kDetUmMma = 0x541,
@@ -147,6 +155,42 @@ __device__ __forceinline__ void um_mma(uint32_t d, uint32_t idesc, uint64_t a, u
                                        uint32_t b_step, bool acc0) {
   for (int s = 0; s < steps; ++s)
     tc_mma_f16(d, a + ((a_step * s) >> 4), b + ((b_step * s) >> 4), idesc, (acc0 || s > 0) ? 1u : 0u);
+}
+
+// One level of the blocked inverse: the blocks (b, c) with b - c = LVL from the levels below.
+//   M_bc = sum_{d=c}^{b-1} A_bd T_dc,  then  T_bc = -T_bb M_bc   (thread: element e = tid + 256 i)
+template <int LVL>
+__device__ __forceinline__ void um_inverse_level(const float* Af, float* Tf, float* Mf, int tid) {
+  constexpr int kBlocks = 4 - LVL;
+#pragma unroll
+  for (int i = 0; i < kBlocks; ++i) {
+    const int e = tid + kUmThreads * i;
+    const int cb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+    const int bb = cb + LVL;
+    float acc = 0.0f;
+#pragma unroll
+    for (int dd = 0; dd < LVL; ++dd) {
+      const int d = cb + dd;
+      const float* arow = Af + (16 * bb + r) * kUmFPitch + 16 * d;
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) acc = __fmaf_rn(arow[kk], Tf[(16 * d + kk) * kUmFPitch + 16 * cb + cc], acc);
+    }
+    Mf[e] = acc;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kBlocks; ++i) {
+    const int e = tid + kUmThreads * i;
+    const int cb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+    const int bb = cb + LVL;
+    const float* trow = Tf + (16 * bb + r) * kUmFPitch + 16 * bb;
+    float acc = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk)
+      if (kk <= r) acc = __fmaf_rn(trow[kk], Mf[(cb << 8) + (kk << 4) + cc], acc);
+    Tf[(16 * bb + r) * kUmFPitch + 16 * cb + cc] = -acc;
+  }
+  __syncthreads();
 }
 
 // One CTA per (value head, sequence); D = 128, bf16 q / k / v / o.
@@ -343,14 +387,15 @@ __global__ void __launch_bounds__(kUmThreads, 1)
         for (int jj = 0; jj < 32; ++jj) {
           const int j = 32 * half + jj;
           Af[t * kUmFPitch + j] =
-              (t < L && j < t) ? __fmul_rn(__fmul_rn(bet[t], expf(__fsub_rn(gam[t], gam[j]))), x[jj]) : 0.0f;
+              (t < L && j < t) ? __fmul_rn(__fmul_rn(bet[t], um_exp_nonpos(__fsub_rn(gam[t], gam[j]))), x[jj]) : 0.0f;
         }
       } else {
         const int t = lrow - kChunk;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
           const int j = 32 * half + jj;
-          x[jj] = (t < L && j <= t) ? __fmul_rn(__fmul_rn(p.scale, expf(__fsub_rn(gam[t], gam[j]))), x[jj]) : 0.0f;
+          x[jj] = (t < L && j <= t) ? __fmul_rn(__fmul_rn(p.scale, um_exp_nonpos(__fsub_rn(gam[t], gam[j]))), x[jj])
+                                    : 0.0f;
         }
         store_split_half(Ph, Pl, t, half, x);
       }
@@ -391,22 +436,20 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     // ---- P5: T = (I + A)^-1 by 16 x 16 blocks, then T rows -> bf16 pair ----
     // diagonal blocks by forward substitution (threads 0-63: block b, column j)
     if (tid < kChunk) {
+      // column j of the block's inverse: x_i = -sum_{k<i} A_ik x_k (x_k = 0 for k < j, x_j = 1),
+      // the sum split over even and odd k to halve the dependent chain
       const int b = tid >> 4, j = tid & 15;
       float x[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        if (i < j) {
-          x[i] = 0.0f;
-        } else if (i == j) {
-          x[i] = 1.0f;
-        } else {
-          float acc = 0.0f;
-          const float* arow = Af + (16 * b + i) * kUmFPitch + 16 * b;
+        const float* arow = Af + (16 * b + i) * kUmFPitch + 16 * b;
+        float e0 = 0.0f, e1 = 0.0f;
 #pragma unroll
-          for (int kk = 0; kk < i; ++kk)
-            if (kk >= j) acc = __fmaf_rn(arow[kk], x[kk], acc);
-          x[i] = -acc;
+        for (int kk = 0; kk < i; kk += 2) {
+          e0 = __fmaf_rn(arow[kk], x[kk], e0);
+          if (kk + 1 < i) e1 = __fmaf_rn(arow[kk + 1], x[kk + 1], e1);
         }
+        x[i] = (i < j) ? 0.0f : ((i == j) ? 1.0f : -__fadd_rn(e0, e1));
       }
 #pragma unroll
       for (int i = 0; i < 16; ++i) Tf[(16 * b + i) * kUmFPitch + 16 * b + j] = x[i];
@@ -416,35 +459,9 @@ __global__ void __launch_bounds__(kUmThreads, 1)
       if ((cc >> 4) > (r >> 4)) Tf[r * kUmFPitch + cc] = 0.0f;   // strictly upper blocks
     }
     __syncthreads();
-#pragma unroll 1
-    for (int lvl = 1; lvl < 4; ++lvl) {
-      const int nblk = 4 - lvl;   // blocks (b, c) with b - c = lvl, c = 0 .. nblk-1
-      // M_bc = sum_{d=c}^{b-1} A_bd T_dc
-      for (int e = tid; e < nblk * 256; e += kUmThreads) {
-        const int cb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-        const int bb = cb + lvl;
-        float acc = 0.0f;
-        for (int d = cb; d < bb; ++d) {
-          const float* arow = Af + (16 * bb + r) * kUmFPitch + 16 * d;
-#pragma unroll
-          for (int kk = 0; kk < 16; ++kk) acc = __fmaf_rn(arow[kk], Tf[(16 * d + kk) * kUmFPitch + 16 * cb + cc], acc);
-        }
-        Mf[e] = acc;
-      }
-      __syncthreads();
-      // T_bc = -T_bb M_bc
-      for (int e = tid; e < nblk * 256; e += kUmThreads) {
-        const int cb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-        const int bb = cb + lvl;
-        const float* trow = Tf + (16 * bb + r) * kUmFPitch + 16 * bb;
-        float acc = 0.0f;
-#pragma unroll
-        for (int kk = 0; kk < 16; ++kk)
-          if (kk <= r) acc = __fmaf_rn(trow[kk], Mf[(cb << 8) + (kk << 4) + cc], acc);
-        Tf[(16 * bb + r) * kUmFPitch + 16 * cb + cc] = -acc;
-      }
-      __syncthreads();
-    }
+    um_inverse_level<1>(Af, Tf, Mf, tid);
+    um_inverse_level<2>(Af, Tf, Mf, tid);
+    um_inverse_level<3>(Af, Tf, Mf, tid);
     if (lrow < kChunk) {
       float x[32];
 #pragma unroll
