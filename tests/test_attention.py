@@ -198,3 +198,23 @@ def test_batch_variant_row_can_diverge_across_batch_sizes(dev):
     batch_out = attention_batch_variant(q_batch, k_batch, v_batch)
     assert not torch.isnan(solo_out).any()
     assert not torch.isnan(batch_out).any()
+
+
+def test_batch_variant_row_diverges_while_invariant_row_does_not(dev):
+    """The variant twin splits a lone sequence's KV over four CTAs but not a sequence inside a
+    64-sequence batch, so the row's bits change with the batch; the invariant kernel's do not.
+    Eight random rows: at least one must differ."""
+    import torch
+    from detkernels_b200.kernels.attention import attention_batch_invariant, attention_batch_variant
+    g = torch.Generator(device=dev).manual_seed(23)
+    q = torch.randn(64, 1, 64, device=dev, generator=g).to(torch.float16)
+    k = torch.randn(64, 1, 1024, 64, device=dev, generator=g).to(torch.float16)
+    v = torch.randn(64, 1, 1024, 64, device=dev, generator=g).to(torch.float16)
+    batch_var = attention_batch_variant(q, k, v)
+    batch_inv = attention_batch_invariant(q, k, v)
+    diverged = 0
+    for r in range(8):
+        one = [x[r:r + 1].contiguous() for x in (q, k, v)]
+        diverged += int(not torch.equal(attention_batch_variant(*one)[0], batch_var[r]))
+        assert torch.equal(attention_batch_invariant(*one)[0], batch_inv[r])
+    assert diverged > 0

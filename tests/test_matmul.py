@@ -181,3 +181,21 @@ def test_matches_cublas_within_bf16_rounding(dev):
     torch.testing.assert_close(got.float(), cub.float(), rtol=2 ** -7, atol=1e-3)
     big = cub.float().abs() > 0.05
     assert np.max(ulp_distance_bf16(got.float()[big].cpu().numpy(), cub.float()[big].cpu().numpy())) <= 2
+
+
+def test_batch_variant_row_diverges_while_invariant_row_does_not(dev):
+    """The failure mode the invariant kernel removes, shown on B200: the variant twin takes a
+    split-K path for a lone row and a direct path inside a 128-row batch, so the same row's
+    bits change with the batch; the invariant kernel's do not.  Several random rows: at least
+    one must differ (the two paths sum 4096 products in different orders)."""
+    import torch
+    from detkernels_b200.kernels.matmul import matmul_batch_invariant, matmul_batch_variant
+    g = torch.Generator(device=dev).manual_seed(21)
+    weight = torch.randn(4096, 512, device=dev, generator=g).to(torch.float16)
+    batch = torch.randn(128, 4096, device=dev, generator=g).to(torch.float16)
+    diverged = 0
+    for r in range(8):
+        row = batch[r:r + 1].contiguous()
+        diverged += int(not torch.equal(matmul_batch_variant(row, weight)[0], matmul_batch_variant(batch, weight)[r]))
+        assert torch.equal(matmul_batch_invariant(row, weight)[0], matmul_batch_invariant(batch, weight)[r])
+    assert diverged > 0

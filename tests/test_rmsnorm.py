@@ -176,3 +176,20 @@ def test_gather_scalar_path_equals_lookup_then_rmsnorm(dev, n_cols, offset):
     x, y = rmsnorm_gather(table, idx, w, 1e-6)
     assert torch.equal(x, table[idx])
     assert torch.equal(y, rmsnorm_batch_invariant(table[idx].contiguous(), w, 1e-6))
+
+
+def test_batch_variant_row_diverges_while_invariant_row_does_not(dev):
+    """The variant twin splits a row's sum of squares over CTAs when the batch is small and not
+    when it is large, so a row's bits change with the batch size; the invariant kernel's do not.
+    Sixteen random rows: at least one must differ."""
+    import torch
+    from detkernels_b200.kernels.rmsnorm import rmsnorm_batch_invariant, rmsnorm_batch_variant
+    g = torch.Generator(device=dev).manual_seed(22)
+    weight = (1 + 0.1 * torch.randn(4096, device=dev, generator=g)).to(torch.float32)
+    batch = torch.randn(64, 4096, device=dev, generator=g).to(torch.float32)
+    diverged = 0
+    for r in range(16):
+        row = batch[r:r + 1].contiguous()
+        diverged += int(not torch.equal(rmsnorm_batch_variant(row, weight)[0], rmsnorm_batch_variant(batch, weight)[r]))
+        assert torch.equal(rmsnorm_batch_invariant(row, weight)[0], rmsnorm_batch_invariant(batch, weight)[r])
+    assert diverged > 0
