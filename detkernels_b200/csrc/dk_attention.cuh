@@ -101,6 +101,14 @@ struct Params {
   int32_t* counters;  // [n_tiles][hkv]
 };
 
+// K and V tensor maps: 64-token boxes for whole blocks and 16-token boxes for the tail of a
+// split whose end falls inside a block, so a row's last block moves only the 16-token groups it
+// needs (a row of ~330 tokens otherwise fetches ~10 % beyond its end).
+struct KvMaps {
+  CUtensorMap k, v, k16, v16;
+};
+constexpr int kTailRows = 16;
+
 enum : int {
   kDetProdEmpty = 0x200,
   kDetFull = 0x201,
@@ -306,7 +314,7 @@ __device__ __forceinline__ int describe_item(const Params& p, int64_t w, Item& i
 // 4 per SM (both measured faster).
 template <typename T, int D, int KM, bool T1>
 __global__ void __launch_bounds__(kThreads, (D == 128 || (!T1 && KM >= 8)) ? 2 : (T1 ? 4 : 3))
-    attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const Params p) {
+    attn_kernel(const __grid_constant__ KvMaps maps, const Params p) {
   using C = Cfg<D, T1>;
   static_assert(KM <= C::KMAX, "merge elements per thread");
   extern __shared__ uint8_t smem_raw[];
@@ -342,8 +350,10 @@ __global__ void __launch_bounds__(kThreads, (D == 128 || (!T1 && KM >= 8)) ? 2 :
     fence_mbar_init();
   }
   if (warp == kConsumerWarps && lane == 0) {
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&maps.k);
+    tma_prefetch_desc(&maps.v);
+    tma_prefetch_desc(&maps.k16);
+    tma_prefetch_desc(&maps.v16);
   }
   pdl_wait();   // lengths, tiles and q may come from the previous kernel
   if (threadIdx.x == 0) pdl_launch_dependents();
@@ -370,15 +380,32 @@ __global__ void __launch_bounds__(kThreads, (D == 128 || (!T1 && KM >= 8)) ? 2 :
           for (int b = 0; b < nblk; ++b) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, kDetProdEmpty, abort_flag)) break;
             uint8_t* st = ring + stage * C::STAGE_BYTES;
-            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
             const int t0 = tb + b * kBlock;
             int tok, slab;
             kv_block_coords(p, it.seq, t0, tok, slab);
+            const int need = min(kBlock, min(tb + kSplit, it.max_len) - t0);   // tokens of the block in use
+            if (need == kBlock) {
+              mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
 #pragma unroll
-            for (int bx = 0; bx < C::NBOX; ++bx) {
-              tma_load_4d(st + bx * C::BOX_BYTES, &tmK, &full[stage], bx * C::BOXD, tok, it.kvh, slab);
-              tma_load_4d(st + C::TENSOR_BYTES + bx * C::BOX_BYTES, &tmV, &full[stage], bx * C::BOXD, tok, it.kvh,
-                          slab);
+              for (int bx = 0; bx < C::NBOX; ++bx) {
+                tma_load_4d(st + bx * C::BOX_BYTES, &maps.k, &full[stage], bx * C::BOXD, tok, it.kvh, slab);
+                tma_load_4d(st + C::TENSOR_BYTES + bx * C::BOX_BYTES, &maps.v, &full[stage], bx * C::BOXD, tok, it.kvh,
+                            slab);
+              }
+            } else {
+              // the block's used 16-token groups only; the consumers mask the rest (K by select,
+              // V rows zeroed) as for tokens past the end of a whole block
+              const int nq = (need + kTailRows - 1) / kTailRows;
+              mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(nq * kTailRows * C::ROWB * C::NBOX * 2));
+              for (int qi = 0; qi < nq; ++qi) {
+#pragma unroll
+                for (int bx = 0; bx < C::NBOX; ++bx) {
+                  const int off = bx * C::BOX_BYTES + qi * kTailRows * C::ROWB;
+                  tma_load_4d(st + off, &maps.k16, &full[stage], bx * C::BOXD, tok + qi * kTailRows, it.kvh, slab);
+                  tma_load_4d(st + C::TENSOR_BYTES + off, &maps.v16, &full[stage], bx * C::BOXD, tok + qi * kTailRows,
+                              it.kvh, slab);
+                }
+              }
             }
             ++fills;
             if (++stage == C::STAGES) {
@@ -585,6 +612,13 @@ __global__ void __launch_bounds__(kThreads, (D == 128 || (!T1 && KM >= 8)) ? 2 :
             ldsm_x4(kbase + k_off[kc], ka[0], ka[1], ka[2], ka[3]);
             mma16816<T>(st, ka, qa[kc][0], qa[kc][1]);
           }
+          // V^T fragments into registers now, so the stage goes back to the producer before the
+          // softmax and the P.V products (the same operands, read earlier)
+          uint32_t vfr[D / 16][4];
+#pragma unroll
+          for (int pc = 0; pc < D / 16; ++pc) ldsm_x4_t(vbase + v_off[pc], vfr[pc][0], vfr[pc][1], vfr[pc][2], vfr[pc][3]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[stage]);
           const int tk = t0 + g;
           float x0 = __fmul_rn(st[0], p.scale_log2);
           float x1 = __fmul_rn(st[2], p.scale_log2);
@@ -621,11 +655,7 @@ __global__ void __launch_bounds__(kThreads, (D == 128 || (!T1 && KM >= 8)) ? 2 :
           }
           // O^T += V^T P^T
 #pragma unroll
-          for (int pc = 0; pc < D / 16; ++pc) {
-            uint32_t va[4];
-            ldsm_x4_t(vbase + v_off[pc], va[0], va[1], va[2], va[3]);
-            mma16816<T>(o[pc], va, pb0, pb1);
-          }
+          for (int pc = 0; pc < D / 16; ++pc) mma16816<T>(o[pc], vfr[pc], pb0, pb1);
         } else {
           // S = Q K^T for this warp's 16 tokens (two n-tiles of 8 tokens).
           float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
@@ -696,8 +726,10 @@ __global__ void __launch_bounds__(kThreads, (D == 128 || (!T1 && KM >= 8)) ? 2 :
             mma16816<T>(o[2 * pc + 1], pa, b0b, b1b);
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
+        if constexpr (!T1) {   // (the single-row path released the stage above)
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[stage]);
+        }
         if (++stage == C::STAGES) {
           stage = 0;
           phase ^= 1u;

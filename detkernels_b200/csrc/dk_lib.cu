@@ -617,8 +617,7 @@ AttnPlan plan_attention(int32_t n_tiles, int32_t rows_per_tile, int32_t hq, int3
 }
 
 template <typename T, int D, int KM, bool T1>
-int attn_launch_km(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int64_t n_items,
-                   cudaStream_t st) {
+int attn_launch_km(const dk::attn::KvMaps& maps, const dk::attn::Params& p, int64_t n_items, cudaStream_t st) {
   using C = dk::attn::Cfg<D, T1>;
   static bool done[kMaxDevices] = {false};
   static int resident[kMaxDevices][dk::attn::kRows + 1] = {};   // CTAs per SM, by rows_cap
@@ -641,19 +640,19 @@ int attn_launch_km(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn:
   const int64_t cap = static_cast<int64_t>(per_sm) * sm_count(dev);
   const int grid = static_cast<int>(n_items < cap ? n_items : cap);
   if (grid <= 0) return DK_OK;
-  cudaError_t e = launch_pdl(fn, dim3(grid), dim3(dk::attn::kThreads), smem, st, tk, tv, p);
+  cudaError_t e = launch_pdl(fn, dim3(grid), dim3(dk::attn::kThreads), smem, st, maps, p);
   if (e != cudaSuccess) return fail(DK_ERR_CUDA, "attention_batch_invariant: launch failed: %s", cudaGetErrorString(e));
   return DK_OK;
 }
 
 template <typename T, int D>
-int attn_launch(const CUtensorMap& tk, const CUtensorMap& tv, const dk::attn::Params& p, int64_t n_items,
+int attn_launch(const dk::attn::KvMaps& maps, const dk::attn::Params& p, int64_t n_items,
                 cudaStream_t st) {
   constexpr int kThr = dk::attn::kConsumerWarps * 32;
   constexpr int kNarrow = (4 < dk::attn::Cfg<D>::KMAX) ? 4 : dk::attn::Cfg<D>::KMAX;
-  if (p.rows_cap == 1) return attn_launch_km<T, D, 1, true>(tk, tv, p, n_items, st);
-  if (p.rows_cap * D <= kNarrow * kThr) return attn_launch_km<T, D, kNarrow, false>(tk, tv, p, n_items, st);
-  return attn_launch_km<T, D, dk::attn::Cfg<D>::KMAX, false>(tk, tv, p, n_items, st);
+  if (p.rows_cap == 1) return attn_launch_km<T, D, 1, true>(maps, p, n_items, st);
+  if (p.rows_cap * D <= kNarrow * kThr) return attn_launch_km<T, D, kNarrow, false>(maps, p, n_items, st);
+  return attn_launch_km<T, D, dk::attn::Cfg<D>::KMAX, false>(maps, p, n_items, st);
 }
 
 template <typename T, int DK, int DV>
@@ -1315,8 +1314,9 @@ int attention_invariant_impl(const void* q, int64_t q_stride_row, int64_t q_stri
     p.counters = static_cast<int32_t*>(workspace);
   }
 
-  // K/V tensor maps: 4-D (d, token, kv head, sequence) -- or (d, token in block, kv head, block)
-  CUtensorMap tk, tv;
+  // K/V tensor maps: 4-D (d, token, kv head, sequence) -- or (d, token in block, kv head, block);
+  // 64-token boxes for whole blocks, 16-token boxes for the tail of a split
+  dk::attn::KvMaps maps;
   const int boxd = head_dim < 64 ? head_dim : 64;
   const uint64_t dims[4] = {static_cast<uint64_t>(head_dim), static_cast<uint64_t>(pg ? pg->page : kv_capacity),
                             static_cast<uint64_t>(n_kv_heads), static_cast<uint64_t>(pg ? pg->n_blocks : kv_n_seq)};
@@ -1325,21 +1325,23 @@ int attention_invariant_impl(const void* q, int64_t q_stride_row, int64_t q_stri
   const uint32_t box[4] = {static_cast<uint32_t>(boxd), static_cast<uint32_t>(dk::attn::kBlock), 1, 1};
   const CUtensorMapSwizzle swz = (boxd == 64) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const CUtensorMapDataType dt = (dtype == DK_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  int rc = encode_map(&tk, dt, 4, k, dims, strides, box, swz, what);
-  if (rc) return rc;
-  rc = encode_map(&tv, dt, 4, v, dims, strides, box, swz, what);
+  const uint32_t box16[4] = {static_cast<uint32_t>(boxd), static_cast<uint32_t>(dk::attn::kTailRows), 1, 1};
+  int rc = encode_map(&maps.k, dt, 4, k, dims, strides, box, swz, what);
+  if (!rc) rc = encode_map(&maps.v, dt, 4, v, dims, strides, box, swz, what);
+  if (!rc) rc = encode_map(&maps.k16, dt, 4, k, dims, strides, box16, swz, what);
+  if (!rc) rc = encode_map(&maps.v16, dt, 4, v, dims, strides, box16, swz, what);
   if (rc) return rc;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t n_items = static_cast<int64_t>(pl.n_tiles) * pl.upt * n_kv_heads;
   if (dtype == DK_BF16) {
-    if (head_dim == 32) return attn_launch<__nv_bfloat16, 32>(tk, tv, p, n_items, st);
-    if (head_dim == 64) return attn_launch<__nv_bfloat16, 64>(tk, tv, p, n_items, st);
-    return attn_launch<__nv_bfloat16, 128>(tk, tv, p, n_items, st);
+    if (head_dim == 32) return attn_launch<__nv_bfloat16, 32>(maps, p, n_items, st);
+    if (head_dim == 64) return attn_launch<__nv_bfloat16, 64>(maps, p, n_items, st);
+    return attn_launch<__nv_bfloat16, 128>(maps, p, n_items, st);
   }
-  if (head_dim == 32) return attn_launch<__half, 32>(tk, tv, p, n_items, st);
-  if (head_dim == 64) return attn_launch<__half, 64>(tk, tv, p, n_items, st);
-  return attn_launch<__half, 128>(tk, tv, p, n_items, st);
+  if (head_dim == 32) return attn_launch<__half, 32>(maps, p, n_items, st);
+  if (head_dim == 64) return attn_launch<__half, 64>(maps, p, n_items, st);
+  return attn_launch<__half, 128>(maps, p, n_items, st);
 }
 
 }  // namespace
