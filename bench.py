@@ -390,11 +390,12 @@ def rmsnorm_roofline(peaks, iters=10):
     return res
 
 
-# DRAM bytes (read + write) per algorithmic byte of the decode attention kernel, from an ncu
-# capture of `python -m detkernels_b200.kernels.benchmark` (B=64, H=8, S=2048, D=64: 270.21 MB
-# of DRAM traffic for 268.57 MB algorithmic); the kernel reads each KV byte once, so traffic
-# scales with the algorithmic bytes of a launch.
-ATTN_DRAM_PER_ALGO_BYTE = 270.21 / 268.57
+# DRAM bytes (read + write) per algorithmic byte of the single-row decode attention kernel, from
+# one ncu capture of a launch at this workload's shape (256 rows, 16 heads, d 64, KV lengths of a
+# mid-decode step: 363.12 MB read + 4.16 MB written for 355.68 MB algorithmic); the kernel reads
+# each KV byte once plus each row's last 16-token group in full, so traffic scales with the
+# algorithmic bytes of a launch.
+ATTN_DRAM_PER_ALGO_BYTE = (363124480 + 4161024) / 355680256
 
 
 # ----------------------------------------------------------------------------- gated delta rule
