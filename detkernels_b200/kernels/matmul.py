@@ -317,7 +317,9 @@ def argmax_finish_parts(gathered_keys, col_offsets, tokens, tokens_copy=None, le
 
     n_parts, n = gathered_keys.shape
     assert gathered_keys.dtype == torch.int64 and gathered_keys.is_contiguous() and gathered_keys.is_cuda
-    assert len(col_offsets) == n_parts and tokens.dtype == torch.int64 and tokens.numel() >= n
+    assert len(col_offsets) == n_parts and tokens.dtype == torch.int64 and tokens.numel() >= n, (
+        "argmax_finish_parts: %d parts with %d column offsets, %d keys per part, tokens %s of %d elements"
+        % (n_parts, len(col_offsets), n, tokens.dtype, tokens.numel()))
     for t in (lens_a, lens_b):
         assert t is None or (t.dtype == torch.int32 and t.numel() >= n)
     for t in (tokens_copy, reset_keys):

@@ -226,9 +226,10 @@ class TPDecodeEngine(DecodeEngine):
 
     def _argmax_step(self, xn, tokens, tokens_copy=None, lens_a=None, lens_b=None):
         """Greedy next token of every row of xn (rows under the final norm) into tokens."""
+        n = xn.shape[0]   # the rows of this step; the key buffers are sized for the engine's capacity
         for sh in self.shards:
             self._mm(xn, sh.w_lm_head, "argmax", argmax_keys=sh.keys)
-        gathered = self._exchange([sh.keys for sh in self.shards])
+        gathered = self._exchange([sh.keys[:n] for sh in self.shards])
         argmax_finish_parts(gathered, self.layout.vocab_offsets, tokens, tokens_copy, lens_a, lens_b,
                             reset_keys=self.shards[0].keys)
         for sh in self.shards[1:]:

@@ -210,6 +210,22 @@ def test_emulated_tp_equals_one_gpu(dev, use_graph):
 
 
 @pytest.mark.gpu
+def test_emulated_tp_with_spare_batch_capacity(dev):
+    """An engine built for more rows than the call's prompts (the serving case): the prefill's
+    greedy step gathers only the prompts' argmax keys and the tokens equal one GPU's."""
+    import torch
+
+    from detkernels_b200.kernels.tiny_model import TinyModel, TinyModelConfig
+    model = TinyModel(TinyModelConfig(**SMALL), device=str(dev))
+    prompts = _prompts(5, SMALL["vocab_size"], 3)
+    want = model.engine(5, 100).generate(prompts, 12)
+    for tp in (2, 4):
+        got = model.tp_engine(tp, 11, 100).generate(prompts, 12)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), tp
+
+
+@pytest.mark.gpu
 def test_emulated_tp_on_the_benchmark_model_128_tokens(dev):
     """The benchmark model's tracked 32-token prompt among 7 ragged prompts: 128 greedy tokens
     at TP = 2, 4, 8 equal TP = 1's for every row."""
