@@ -10,11 +10,13 @@
 //   D[n, m] = sum_k B[k, n] * A[m, k]
 // with the 128 weight columns of a tile on the UMMA M axis (B read MN-major,
 // straight from its row-major [K, N] layout) and 128 tokens on the UMMA N axis
-// (A read K-major).  The tile shape (128 x 128 x 16 per instruction) is the
-// same for every M.  When all M rows fit one 128-token tile, the activation
-// TMA box covers only ceil8(M) rows; the instruction still spans 128 token
-// columns and columns beyond the box read stale shared memory.  Each output
-// column depends only on its own token row, and stale columns are never stored.
+// (A read K-major).  The tile is 128 weight columns x 128 tokens for every M.
+// When all M rows fit one 128-token tile, the activation TMA box covers only
+// ceil8(M) rows and the instruction spans ceil16(M) token columns (an element's
+// bits do not depend on the instruction's N); a column beyond the box reads
+// stale shared memory.  Each output column depends only on its own token row,
+// stale columns are never stored, and the epilogue skips 32-token chunks that
+// hold no token below M.
 //
 // Fixed reduction structure (the definition of the output bits):
 //   * K is cut into DK_MATMUL_K_SLICES = 8 slices of L = ceil16(ceil(K/8))
@@ -584,7 +586,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t use_par = 0;   // bit k: parity of the number of times slot k has been written
       int ordinal = 0;
-      constexpr uint32_t idesc = umma_idesc_f16(FMT, /*a_mn=*/1, /*b_mn=*/0, kTileN, kTileM);
+      // token columns per instruction: the loaded rows rounded up to 16 (an element's bits do not
+      // depend on the instruction's N), so a few decode tokens do not read 128 rows of operand
+      const uint32_t n_mma = static_cast<uint32_t>((p.a_rows + 15) / 16 * 16);
+      const uint32_t idesc = umma_idesc_f16(FMT, /*a_mn=*/1, /*b_mn=*/0, kTileN, n_mma);
       for (int u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++ordinal) {
         const int g = u % n_groups;
         for (int si = 0; si < p.group && !abort_flag; ++si) {
@@ -652,6 +657,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(p, t, mt, nt);
       const int n = nt * kTileN + n_local;
       const int m0 = mt * kTileM + col0;
+      // 32-token chunks of this thread's columns that hold tokens below M (warp-uniform): the
+      // others are never stored, so their partial sums are neither read nor folded
+      const int c_end = (p.M > m0) ? min(kEpiCols / 32, (p.M - m0 + 31) / 32) : 0;
       const bool n_ok = n < p.N;
       Params q = p;
       if (p.mode == SPLIT) q.ws = p.ws + static_cast<int64_t>(g) * MN;
@@ -675,8 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float z[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) z[j] = 0.0f;
-#pragma unroll
-            for (int c = 0; c < kEpiCols / 32; ++c) tmem_st_32x32b_x32(x_addr + c * 32, z);
+            for (int c = 0; c < c_end; ++c) tmem_st_32x32b_x32(x_addr + c * 32, z);
             tmem_st_wait();
           }
           stack = (stack & ~3u) | static_cast<uint32_t>(slot);
@@ -684,7 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int res_slot = (nlev > 0) ? static_cast<int>((stack >> (2 * (nlev - 1))) & 3u) : slot;
 #pragma unroll 1
-        for (int c = 0; c < kEpiCols / 32; ++c) {
+        for (int c = 0; c < c_end; ++c) {
           float acc[32];
           if (empty_slice) {
 #pragma unroll
