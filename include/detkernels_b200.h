@@ -118,7 +118,9 @@ int dk_rmsnorm_batch_variant(const void* x, int64_t x_row_stride, const void* we
  * steps into its own f32 TMEM accumulator (partial p_s), then summed along the
  * fixed tree ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)) and rounded to the dtype. */
 
-/* Scratch bytes the invariant / variant matmul may need for this shape. */
+/* Scratch bytes the invariant / variant matmul may need for this shape: f32 subtree sums when
+ * the schedule splits K over CTAs, and for large token counts (the CTA-pair kernel) a 128 KB
+ * stash per resident CTA for the left half of the slice tree.  0 means no workspace is needed. */
 size_t dk_matmul_workspace_size(int64_t M, int64_t N, int64_t K);
 /* replaces kernels/matmul.py:161-186 matmul_batch_invariant (+ _matmul_kernel 64-100) */
 int dk_matmul_batch_invariant(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
