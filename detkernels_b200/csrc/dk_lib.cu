@@ -167,6 +167,13 @@ int rmsnorm_inv_launch(const void* x, int64_t xs, const void* w, void* y, int64_
     // rows of 3-4 chunks per thread (12-16 KB: 4096 f32, 8192 16-bit elements): streamed by
     // persistent CTAs that hold the next row in registers.  Shorter rows keep one CTA per row.
     e = rmsnorm_stream<T, W, 4>(x, xs, w, y, ys, rows, cols, eps, st);
+  } else if (vec && cols / VEC <= 128 && rows >= 2LL * dk::kRmsHalfPerSm * sm_count(current_device())) {
+    // many short rows (at most 128 chunks): persistent CTAs, a row per 128-thread half
+    const int64_t cap = static_cast<int64_t>(dk::kRmsHalfPerSm) * sm_count(current_device());
+    const int64_t want = (rows + 1) / 2;
+    e = launch_pdl(dk::rmsnorm_inv_half_kernel<T, W>, dim3(static_cast<unsigned>(want < cap ? want : cap)),
+                   dim3(dk::kRmsThreads), 0, st, static_cast<const T*>(x), xs, static_cast<const W*>(w),
+                   static_cast<T*>(y), ys, rows, cols, eps);
   } else if (vec) {
     constexpr int MAXC = (sizeof(T) == 4) ? 8 : 4;
     e = launch_pdl(dk::rmsnorm_inv_vec_kernel<T, W, MAXC>, grid, dim3(dk::kRmsThreads), 0, st,

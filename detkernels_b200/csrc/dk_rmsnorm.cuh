@@ -185,6 +185,83 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_inv_stream_kernel(const T
   }
 }
 
+// Streaming form of rmsnorm_inv_vec_kernel for many short rows (at most 128 16-byte chunks: 1024
+// 16-bit or 512 f32 elements): each half of a persistent CTA (128 threads) walks its own rows, one
+// chunk per thread, with the chunks of the next two rows loaded before the current row is reduced
+// (6 CTAs per SM: 1536 threads, 48 bytes each in flight).  In the
+// 256-thread kernel such a row's chunks all belong to threads 0-127, so warps 4-7 contribute exact
+// zeros and its cross-warp butterfly (4, 2, 1) reduces to this half's (2, 1) over the same four
+// warp sums in the same order: the bits are those of the vector kernel.
+constexpr int kRmsHalfPerSm = 6;
+
+// Barrier among the 128 threads of one half of the CTA (named barriers 1 and 2).
+__device__ __forceinline__ void half_sync(int half) {
+  if (half == 0) {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+  } else {
+    asm volatile("bar.sync 2, 128;" ::: "memory");
+  }
+}
+
+template <typename T, typename W>
+__global__ void __launch_bounds__(kRmsThreads, kRmsHalfPerSm) rmsnorm_inv_half_kernel(const T* __restrict__ x, int64_t xs,
+                                                                        const W* __restrict__ w,
+                                                                        T* __restrict__ y, int64_t ys,
+                                                                        int64_t n_rows, int64_t n_cols, float eps) {
+  __shared__ float red[2][5];
+  constexpr int VEC = Vec16<T>::N;
+  const int half = threadIdx.x >> 7;
+  const int ht = threadIdx.x & 127;
+  const int lane = threadIdx.x & 31, hw = ht >> 5;
+  const int64_t nchunks = n_cols / VEC;
+  const bool mine = ht < nchunks;
+  pdl_wait();   // x may come from the previous kernel
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  const int64_t stride = 2 * static_cast<int64_t>(gridDim.x);
+  int64_t row = 2 * static_cast<int64_t>(blockIdx.x) + half;
+  uint4 cur = make_uint4(0u, 0u, 0u, 0u), nxt = cur, nxt2 = cur;
+  if (row < n_rows && mine) cur = __ldcs(reinterpret_cast<const uint4*>(x + row * xs) + ht);
+  if (row + stride < n_rows && mine) nxt = __ldcs(reinterpret_cast<const uint4*>(x + (row + stride) * xs) + ht);
+  for (; row < n_rows; row += stride) {
+    const int64_t nrow = row + 2 * stride;
+    if (nrow < n_rows && mine) nxt2 = __ldcs(reinterpret_cast<const uint4*>(x + nrow * xs) + ht);
+    float acc = 0.0f;
+    const Vec16<T> v = *reinterpret_cast<const Vec16<T>*>(&cur);
+    if (mine) {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float f = to_f32<T>(v.v[j]);
+        acc = __fmaf_rn(f, f, acc);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) red[half][hw] = acc;
+    half_sync(half);
+    if (hw == 0) {
+      float t = (lane < 4) ? red[half][lane] : 0.0f;
+      t += __shfl_xor_sync(0xffffffffu, t, 2);
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+      if (lane == 0) red[half][4] = t;
+    }
+    half_sync(half);
+    const float total = red[half][4];
+    const float var = __fdiv_rn(total, (float)n_cols);
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    if (mine) {
+      Vec16<T> o;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float xn = __fmul_rn(to_f32<T>(v.v[j]), rstd);
+        o.v[j] = from_f32<T>(__fmul_rn(xn, to_f32<W>(w[ht * VEC + j])));
+      }
+      __stcs(reinterpret_cast<uint4*>(y + row * ys) + ht, *reinterpret_cast<const uint4*>(&o));
+    }
+    cur = nxt;
+    nxt = nxt2;
+  }
+}
+
 // Embedding lookup fused into the invariant RMSNorm: row r reads table row idx[r], copies it
 // to x_out (the residual stream) and normalises it with exactly rmsnorm_inv_vec_kernel's
 // arithmetic.  An index outside [0, table_rows) records DK_ERR_DEVICE_CHECK and leaves the

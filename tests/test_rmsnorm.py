@@ -193,3 +193,24 @@ def test_batch_variant_row_diverges_while_invariant_row_does_not(dev):
         diverged += int(not torch.equal(rmsnorm_batch_variant(row, weight)[0], rmsnorm_batch_variant(batch, weight)[r]))
         assert torch.equal(rmsnorm_batch_invariant(row, weight)[0], rmsnorm_batch_invariant(batch, weight)[r])
     assert diverged > 0
+
+
+@pytest.mark.parametrize("dtype_name,w_name,cols", [("bfloat16", "bfloat16", 1024), ("float16", "float32", 1000),
+                                                    ("float32", "float32", 512), ("bfloat16", "float32", 8)])
+def test_many_short_rows_equal_the_one_row_per_cta_bits(dev, dtype_name, w_name, cols):
+    """A large batch of short rows (at most 128 16-byte chunks) runs on persistent CTAs, a row per
+    128-thread half; a batch below the size threshold runs one CTA per row.  The same rows give
+    the same bits on both paths."""
+    import torch
+    from detkernels_b200.kernels.rmsnorm import rmsnorm_batch_invariant
+    dt, wt = getattr(torch, dtype_name), getattr(torch, w_name)
+    g = torch.Generator(device=dev).manual_seed(cols)
+    x = (3 * torch.randn(5001, cols, device=dev, generator=g)).to(dt)
+    w = (1 + 0.1 * torch.randn(cols, device=dev, generator=g)).to(wt)
+    many = rmsnorm_batch_invariant(x, w)
+    few = rmsnorm_batch_invariant(x[:1000].contiguous(), w)
+    torch.cuda.synchronize()
+    assert torch.equal(many[:1000], few)
+    want = oracle.rmsnorm(x.float().cpu().numpy(), w.float().cpu().numpy(), 1e-6, dtype_name)
+    tol = {"float32": (2e-6, 1e-6), "bfloat16": (2 ** -7, 2 ** -7), "float16": (2 ** -10, 2 ** -10)}[dtype_name]
+    np.testing.assert_allclose(many.float().cpu().numpy(), want, rtol=tol[0], atol=tol[1])
