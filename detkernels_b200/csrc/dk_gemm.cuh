@@ -241,16 +241,44 @@ __device__ __forceinline__ void store_final(const Params& p, T* C, int m, int n,
 // Argmax key of the rounded value v at column n: larger key = larger value, and among equal values
 // the smaller column.  NaN sorts above everything; -0 and +0 are equal.  Every real key is > 0.
 template <typename T>
-__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
+__device__ __forceinline__ uint32_t argmax_hi(float v) {
   const float r = rnd<T>(v);
-  uint32_t hi;
-  if (r != r) {
-    hi = 0xffffffffu;
-  } else {
-    const uint32_t b = __float_as_uint(r == 0.0f ? 0.0f : r);
-    hi = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  if (r != r) return 0xffffffffu;
+  const uint32_t b = __float_as_uint(r == 0.0f ? 0.0f : r);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+template <typename T>
+__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
+  return (static_cast<unsigned long long>(argmax_hi<T>(v)) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(n));
+}
+
+// The largest argmax_key of columns n_base .. n_base + ncols - 1 with values v[0..ncols) (0 when
+// ncols <= 0).  Four independent running maxima (column k goes to k % 4, a strictly larger value
+// replaces, so each keeps its first maximal column) merged at the end: the same key as a serial
+// max over the 32 keys, without its 32-long dependent chain of 64-bit compares.
+template <typename T>
+__device__ __forceinline__ unsigned long long argmax_chunk_key(const float (&v)[32], int ncols, int n_base) {
+  uint32_t bh[4] = {0u, 0u, 0u, 0u};
+  int bk[4] = {0, 1, 2, 3};
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const uint32_t h = (k < ncols) ? argmax_hi<T>(v[k]) : 0u;   // every real hi is > 0
+    if (h > bh[k & 3]) {
+      bh[k & 3] = h;
+      bk[k & 3] = k;
+    }
   }
-  return (static_cast<unsigned long long>(hi) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(n));
+  uint32_t h = bh[0];
+  int kk = bk[0];
+#pragma unroll
+  for (int i = 1; i < 4; ++i) {
+    if (bh[i] > h || (bh[i] == h && bk[i] < kk)) {
+      h = bh[i];
+      kk = bk[i];
+    }
+  }
+  return h ? ((static_cast<unsigned long long>(h) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(n_base + kk)))
+           : 0ull;
 }
 
 // Max over the 32 lanes (columns) of each of 32 token values k[0..31]; lane L ends with token L's
@@ -328,14 +356,7 @@ __device__ __forceinline__ void store_final_row(const Params& p, T* C, int m, in
   const bool full = (ncols == 32);
   switch (e.mode) {
     case DK_EPI_ARGMAX: {
-      unsigned long long best = 0ull;
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        if (k < ncols) {
-          const unsigned long long key = argmax_key<T>(v[k], n_base + k);
-          best = key > best ? key : best;
-        }
-      }
+      const unsigned long long best = argmax_chunk_key<T>(v, ncols, n_base);
       if (best != 0ull) atomicMax(e.argmax_keys + m, best);
       if (!C) return;
       break;   // logits stored as plain values below

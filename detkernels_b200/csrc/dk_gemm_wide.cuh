@@ -126,13 +126,8 @@ __device__ __forceinline__ void wide_emit(const Params& q, float* ws, T* C, int 
   if (m >= q.M || ncols <= 0) return;
   if constexpr (FOLDK) {
     if (q.epi.mode == DK_EPI_ARGMAX) {
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        if (k < ncols) {
-          const unsigned long long key = argmax_key<T>(v[k], n_base + k);
-          best = key > best ? key : best;
-        }
-      }
+      const unsigned long long key = argmax_chunk_key<T>(v, ncols, n_base);
+      best = key > best ? key : best;
       if (C) {
         float w[32];
 #pragma unroll
@@ -268,23 +263,31 @@ __device__ __forceinline__ void wide_epilogue(const Params& p, uint64_t* slot_fu
       if (si + 1 == p.group) {
         unsigned long long best = 0ull;
         if (p.group == 8) {
+          // final = S + R: the stash is read two chunks at a time, all of it before any store,
+          // so its L2 round trips overlap instead of one per chunk between the stores
 #pragma unroll
-          for (int c = 0; c < kWideChunks; ++c) {
-            float v[32];
+          for (int c = 0; c < kWideChunks; c += 2) {
+            float4 s0[8], s1[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const float4 s4 = __ldcg(stash + (c * 8 + j) * 128);
-              v[4 * j] = __fadd_rn(s4.x, R[c][4 * j]);
-              v[4 * j + 1] = __fadd_rn(s4.y, R[c][4 * j + 1]);
-              v[4 * j + 2] = __fadd_rn(s4.z, R[c][4 * j + 2]);
-              v[4 * j + 3] = __fadd_rn(s4.w, R[c][4 * j + 3]);
+              s0[j] = __ldcg(stash + (c * 8 + j) * 128);
+              s1[j] = __ldcg(stash + ((c + 1) * 8 + j) * 128);
             }
-            wide_emit<T, FOLDK>(p, ws, C, m, n0 + c * 32, v, best);
-          }
-        } else {
 #pragma unroll
-          for (int c = 0; c < kWideChunks; ++c) wide_emit<T, FOLDK>(p, ws, C, m, n0 + c * 32, R[c], best);
+            for (int j = 0; j < 8; ++j) {
+              R[c][4 * j] = __fadd_rn(s0[j].x, R[c][4 * j]);
+              R[c][4 * j + 1] = __fadd_rn(s0[j].y, R[c][4 * j + 1]);
+              R[c][4 * j + 2] = __fadd_rn(s0[j].z, R[c][4 * j + 2]);
+              R[c][4 * j + 3] = __fadd_rn(s0[j].w, R[c][4 * j + 3]);
+              R[c + 1][4 * j] = __fadd_rn(s1[j].x, R[c + 1][4 * j]);
+              R[c + 1][4 * j + 1] = __fadd_rn(s1[j].y, R[c + 1][4 * j + 1]);
+              R[c + 1][4 * j + 2] = __fadd_rn(s1[j].z, R[c + 1][4 * j + 2]);
+              R[c + 1][4 * j + 3] = __fadd_rn(s1[j].w, R[c + 1][4 * j + 3]);
+            }
+          }
         }
+#pragma unroll
+        for (int c = 0; c < kWideChunks; ++c) wide_emit<T, FOLDK>(p, ws, C, m, n0 + c * 32, R[c], best);
         if constexpr (FOLDK) {
           if (p.epi.mode == DK_EPI_ARGMAX && best != 0ull) atomicMax(p.epi.argmax_keys + m, best);
         }

@@ -117,6 +117,27 @@ def test_argmax_matches_torch_argmax_including_ties(dev, dtype_name, mkn):
         assert torch.equal(tok, want)
 
 
+@pytest.mark.parametrize("mkn", [(256, 1024, 32000), (7, 512, 1000), (300, 256, 4096)])
+def test_argmax_ties_inside_one_32_column_chunk(dev, mkn):
+    """Equal maxima at columns 7 and 8 (one 32-column chunk, different running maxima of the
+    chunk reduction) and 40 (the next chunk): the smallest column wins, as torch.argmax."""
+    import torch
+    from detkernels_b200.kernels.matmul import argmax_finish, matmul_batch_invariant, matmul_fused
+    m, k, n = mkn
+    a, w = _inputs(dev, m, k, n, torch.bfloat16, seed=9)
+    a = a.abs()
+    for col in (8, 7, 40):
+        w[:, col] = 0.25
+    logits = matmul_batch_invariant(a, w)
+    keys = torch.zeros(m, dtype=torch.int64, device=dev)
+    tok = torch.empty(m, dtype=torch.int64, device=dev)
+    matmul_fused(a, w, "argmax", argmax_keys=keys)
+    argmax_finish(keys, tok)
+    want = logits.argmax(dim=-1)
+    assert torch.equal(tok, want)
+    assert bool((want == 7).all())
+
+
 def test_fused_rows_are_batch_invariant(dev):
     """A row's fused result does not depend on the other rows (M = 1 vs 256)."""
     import torch
