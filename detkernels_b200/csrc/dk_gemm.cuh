@@ -713,20 +713,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int res_slot = (nlev > 0) ? static_cast<int>((stack >> (2 * (nlev - 1))) & 3u) : slot;
 #pragma unroll 1
         for (int c = 0; c < c_end; ++c) {
+          // this slice's chunk and the pending left operand of the first level it closes, read
+          // before one wait; further levels (groups of 4 and 8) are read one at a time
           float acc[32];
+          float left[32];
+          if (!empty_slice) tmem_ld_32x32b_x32(x_addr + c * 32, acc);
+          if (nlev > 0) tmem_ld_32x32b_x32(lane_base + (stack & 3u) * kTileM + c * 32, left);
+          tmem_ld_wait();
           if (empty_slice) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-          } else {
-            tmem_ld_32x32b_x32(x_addr + c * 32, acc);
-            tmem_ld_wait();
           }
           // close the tree levels: acc = stack[l] + acc for l = 0 .. nlev-1
+          if (nlev > 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(left[j], acc[j]);
+          }
 #pragma unroll 1
-          for (int l = 0; l < nlev; ++l) {
-            float left[32];
-            const uint32_t ls = (stack >> (2 * l)) & 3u;
-            tmem_ld_32x32b_x32(lane_base + ls * kTileM + c * 32, left);
+          for (int l = 1; l < nlev; ++l) {
+            tmem_ld_32x32b_x32(lane_base + ((stack >> (2 * l)) & 3u) * kTileM + c * 32, left);
             tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(left[j], acc[j]);
