@@ -602,6 +602,14 @@ def run_ours(args, rank, world, local):
             if not torch.equal(o[0], solo):
                 divergences += 1
 
+    # ---- in-graph decode matmul times: one more run, untimed, whose decode graph brackets every
+    # matmul (with its split-K fold) by events; the events end those launches' programmatic
+    # overlap, which is why the timed steps carry none ----
+    gemm_times = None
+    if tp == 1:
+        eng.run(plan, NEW_TOKENS, gemm_timing=True)
+        gemm_times = eng.gemm_times_ms()
+
     # ---- end-to-end through the public API with host buffers ----
     for _ in range(0 if args.skip_e2e else 2):   # warm the public path (graph captured on first use)
         model.generate(prompts, NEW_TOKENS, "batch_invariant", **gen_kw).cpu()
@@ -652,6 +660,8 @@ def run_ours(args, rank, world, local):
                 "algorithmic_bytes_per_launch": int(avg_bytes),
                 "share_of_step": round(attn_ms / ms_per_step, 3)}
 
+    decode_gemm = decode_gemm_table(gemm_times, eng, len(prompts), peaks) if gemm_times else None
+
     cpu = cpu_baseline_sample() if world == 1 and not args.skip_cpu else None
     _, cpu_toks = (cpu_sample(cpu_sample_prompts(), 16, model) if world == 1 and not args.skip_cpu
                    else (None, None))
@@ -682,11 +692,38 @@ def run_ours(args, rank, world, local):
         "divergences": divergences,
         "parity": parity,
         "gemm_vs_cublas": gemm,
+        "decode_gemm": decode_gemm,
         "rmsnorm_roofline": rms,
         "gdn": gdn,
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def decode_gemm_table(times, eng, rows, peaks):
+    """Per matmul family of the decode step (times from events inside the decode graph, each
+    launch with its split-K fold): mean µs per launch, the weight bytes it streams, and those
+    bytes per second against the HBM peak (the weights are the matmul's algorithmic bytes: the
+    activations of 256 rows are < 6 % of them)."""
+    weights = {"qkv": eng.layers[0]["w_qkv"], "o": eng.layers[0]["w_o"],
+               "gate_up": eng.layers[0].get("w_gu", eng.layers[0].get("w_mlp1")), "down": eng.layers[0]["w_mlp2"],
+               "lm_head": eng.model.w_lm_head}
+    out = {}
+    step_us = 0.0
+    n_steps = NEW_TOKENS - 1
+    for label, ms in times.items():
+        w = weights.get(label)
+        if w is None or not ms:
+            continue
+        us = 1e3 * sum(ms) / len(ms)
+        wb = w.numel() * w.element_size()
+        out[label] = {"launches_per_step": round(len(ms) / n_steps, 2), "us": round(us, 2), "weight_bytes": int(wb),
+                      "achieved_gbs": round(wb / (us * 1e-6) / 1e9, 1),
+                      "frac_hbm": round(wb / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4),
+                      "tflops": round(2.0 * rows * w.numel() / (us * 1e-6) / 1e12, 1)}
+        step_us += us * len(ms) / n_steps
+    out["per_decode_step_us"] = round(step_us, 1)
+    return out
 
 
 def main(argv=None):

@@ -356,6 +356,8 @@ class DecodeEngine:
         self.argmax_keys = torch.zeros(self.B, dtype=torch.int64, device=dev)
         self._graphs = {}
         self._last_events = None
+        self._gemm_events = None        # list of (label, start, end) while a GEMM-timing graph is captured
+        self._last_gemm_events = None
         # explicit scratch so captured graphs never allocate
         self._lib = _lib
         lib = _lib.load()
@@ -369,8 +371,20 @@ class DecodeEngine:
         self.attn_ws = torch.zeros(max(a_ws, 1), dtype=torch.uint8, device=dev)
 
     # ---------------- building blocks (all per-row) ----------------
-    def _mm(self, x, w, epilogue="store", **kw):
-        return matmul_fused(x, w, epilogue, workspace=self.gemm_ws, **kw)
+    def _mm(self, x, w, epilogue="store", label=None, **kw):
+        """matmul_fused on the engine's workspace; while a GEMM-timing graph is being captured,
+        the call (the GEMM and its split-K fold) is bracketed by external events under `label`."""
+        ev = getattr(self, "_gemm_events", None)
+        if ev is None or label is None:
+            return matmul_fused(x, w, epilogue, workspace=self.gemm_ws, **kw)
+        import torch
+        s, e = (torch.cuda.Event(enable_timing=True, external=True),
+                torch.cuda.Event(enable_timing=True, external=True))
+        s.record()
+        out = matmul_fused(x, w, epilogue, workspace=self.gemm_ws, **kw)
+        e.record()
+        ev.append((label, s, e))
+        return out
 
     def _next_norm_w(self, li):
         """The RMSNorm weight applied to block li's output: block li+1's input norm, or the final norm."""
@@ -387,7 +401,8 @@ class DecodeEngine:
         R = x.shape[0]
         H, D = self.H, self.D
         q = self._mm(xn, layer["w_qkv"], "qkv_cache", q_cols=H * D, head_dim=D, k_cache=self.k_cache[li],
-                     v_cache=self.v_cache[li], row_seq=write_seq, row_pos=write_pos, block_table=self.block_table)
+                     v_cache=self.v_cache[li], row_seq=write_seq, row_pos=write_pos, block_table=self.block_table,
+                     label="qkv")
         if events is not None:
             events[0].record()
         attn = attention_decode(q.view(R, H, D), self.k_cache[li], self.v_cache[li], q_lens, row_tiles=row_tiles,
@@ -396,14 +411,14 @@ class DecodeEngine:
             events[1].record()
         xn = torch.empty_like(x)
         x = self._mm(attn.reshape(R, H * D), layer["w_o"], "residual_rmsnorm", residual=x,
-                     norm_weight=layer["norm2_w"], norm_out=xn, eps=cfg.eps)
+                     norm_weight=layer["norm2_w"], norm_out=xn, eps=cfg.eps, label="o")
         if cfg.mlp == "swiglu":
-            hid = self._mm(xn, layer["w_gu"], "silu_mul")
+            hid = self._mm(xn, layer["w_gu"], "silu_mul", label="gate_up")
         else:
-            hid = self._mm(xn, layer["w_mlp1"], "silu")
+            hid = self._mm(xn, layer["w_mlp1"], "silu", label="gate_up")
         xn_next = torch.empty_like(x)
         x = self._mm(hid, layer["w_mlp2"], "residual_rmsnorm", residual=x, norm_weight=self._next_norm_w(li),
-                     norm_out=xn_next, eps=cfg.eps)
+                     norm_out=xn_next, eps=cfg.eps, label="down")
         return x, xn_next
 
     def _logits(self, xn):
@@ -516,12 +531,14 @@ class DecodeEngine:
                       torch.cuda.Event(enable_timing=True, external=True))
                 events.append(ev)
             x, xn = self._layer(li, layer, x, xn, None, self.kv_lens, self.q_lens, None, max_len, self.attn_ws, ev)
-        self._mm(xn, self.model.w_lm_head, "argmax", argmax_keys=self.argmax_keys)
+        self._mm(xn, self.model.w_lm_head, "argmax", argmax_keys=self.argmax_keys, label="lm_head")
         argmax_finish(self.argmax_keys, self.tokens, out_row, self.kv_lens, self.q_lens)
         return self.tokens
 
-    def _capture(self, n_steps, start_len, timing):
-        """Capture n_steps decode steps (one graph) starting from rows of length <= start_len."""
+    def _capture(self, n_steps, start_len, timing, gemm_timing=False):
+        """Capture n_steps decode steps (one graph) starting from rows of length <= start_len.
+        timing: events around every attention launch; gemm_timing: around every matmul (with
+        its fold).  Both end the programmatic overlap of the launches they bracket."""
         import torch
 
         out = torch.empty((n_steps, self.B), dtype=torch.long, device=self.device)
@@ -535,16 +552,21 @@ class DecodeEngine:
         self.kv_lens.copy_(saved[1])
         self.q_lens.copy_(saved[2])
         events = [] if timing else None
+        gemm_events = [] if gemm_timing else None
         g = torch.cuda.CUDAGraph()
         n0 = self._lib.launch_count()
-        with torch.cuda.graph(g):
-            for t in range(n_steps):
-                self._decode_step(min(start_len + t + 1, self.S), out[t], events)
+        self._gemm_events = gemm_events
+        try:
+            with torch.cuda.graph(g):
+                for t in range(n_steps):
+                    self._decode_step(min(start_len + t + 1, self.S), out[t], events)
+        finally:
+            self._gemm_events = None
         n_graph = self._lib.launch_count() - n0
         self._lib.count_launch(-n_graph)  # recorded, not executed; counted at each replay
-        return g, out, events, n_graph
+        return g, out, events, n_graph, gemm_events
 
-    def decode(self, n_steps: int, start_len: Optional[int] = None, timing: bool = False):
+    def decode(self, n_steps: int, start_len: Optional[int] = None, timing: bool = False, gemm_timing: bool = False):
         """Run n_steps decode steps from the current tokens/kv_lens; returns [n_steps, B]
         (device).  start_len bounds the current kv_lens (defaults to the capacity).
         With timing=True, per-launch attention durations of the run are available
@@ -563,15 +585,16 @@ class DecodeEngine:
             for t in range(n_steps):
                 self._decode_step(min(start_len + t + 1, self.S), out[t])
             return out
-        key = (n_steps, start_len, timing)
+        key = (n_steps, start_len, timing, gemm_timing)
         if key not in self._graphs:
             while len(self._graphs) >= self.MAX_GRAPHS:     # oldest capture first
                 self._graphs.pop(next(iter(self._graphs)))
-            self._graphs[key] = self._capture(n_steps, start_len, timing)
-        g, out, events, n_graph = self._graphs[key]
+            self._graphs[key] = self._capture(n_steps, start_len, timing, gemm_timing)
+        g, out, events, n_graph, gemm_events = self._graphs[key]
         g.replay()
         self._lib.count_launch(n_graph)
         self._last_events = events
+        self._last_gemm_events = gemm_events
         return out
 
     def attention_times_ms(self):
@@ -583,7 +606,19 @@ class DecodeEngine:
         evs[-1][1].synchronize()
         return [a.elapsed_time(b) for a, b in evs]
 
-    def run(self, plan, n_steps: int, timing: bool = False, before_decode=None):
+    def gemm_times_ms(self):
+        """{label: [ms, ...]} of every matmul launch (with its fold) of the last decode run with
+        gemm_timing=True; labels qkv, o, gate_up, down, lm_head."""
+        evs = self._last_gemm_events or []
+        if not evs:
+            return {}
+        evs[-1][2].synchronize()
+        out = {}
+        for label, s, e in evs:
+            out.setdefault(label, []).append(s.elapsed_time(e))
+        return out
+
+    def run(self, plan, n_steps: int, timing: bool = False, before_decode=None, gemm_timing: bool = False):
         """Prefill + greedy decode; returns [B, n_steps] generated ids (device).
         before_decode (optional) is called on the host after the prefill has been
         queued and before the decode graph is launched."""
@@ -602,7 +637,7 @@ class DecodeEngine:
         self.tokens[:B] = first
         if before_decode is not None:
             before_decode()
-        rest = self.decode(n_steps - 1, start_len=plan["max_len"], timing=timing)
+        rest = self.decode(n_steps - 1, start_len=plan["max_len"], timing=timing, gemm_timing=gemm_timing)
         return torch.cat([first[:, None], rest[:, :B].t()], dim=1)
 
     def generate(self, prompts: Sequence[Sequence[int]], n_steps: int):

@@ -131,3 +131,23 @@ def test_baseline_decode_config_tracked_prompt_bitwise(dev):
         if ref is None:
             ref = row
         assert torch.equal(row, ref), n_other
+
+
+def test_gemm_timing_graph_gives_the_same_tokens_and_one_time_per_matmul(dev):
+    """A decode graph captured with events around every matmul (bench.py's in-graph GEMM
+    times) generates the same tokens as the plain graph and times each matmul family once per
+    layer and step (the LM head once per step)."""
+    import torch
+    model = _small_model(dev, mlp="swiglu", dtype="bfloat16")
+    prompts = [[1, 2, 3], [4, 5, 6, 7, 8], [9]]
+    eng = model.engine(len(prompts), 32)
+    plan = eng.plan(prompts)
+    want = eng.run(plan, 6)
+    got = eng.run(plan, 6, gemm_timing=True)
+    assert torch.equal(got, want)
+    times = eng.gemm_times_ms()
+    L, steps = model.config.num_layers, 5
+    assert sorted(times) == ["down", "gate_up", "lm_head", "o", "qkv"]
+    for label, ms in times.items():
+        assert len(ms) == (steps if label == "lm_head" else L * steps), label
+        assert all(t > 0 for t in ms)
