@@ -1,5 +1,5 @@
 """Decode attention: the reference's test pattern (tests/test_attention.py),
-oracle parity with GQA and ragged KV lengths, the BASELINE invariance config
+oracle parity with GQA and ragged KV lengths, the headline invariance config
 (q [B, 32, 128], 8 kv heads, L ~ U[128, 8192], B in {1, 8, 64, 256}), and
 prefill row tiles reproducing decode rows bit for bit."""
 import numpy as np

@@ -1,5 +1,5 @@
 """Matmul: the reference's test pattern (tests/test_matmul.py) on the tcgen05
-GEMM, oracle parity, the BASELINE invariance sweep (row 0 across M in
+GEMM, oracle parity, the headline invariance sweep (row 0 across M in
 {1, 8, 64, 256, 2048}, N in {4096, 11008}) and the slice/fold decomposition
 used by tensor parallelism."""
 import numpy as np

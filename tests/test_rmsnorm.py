@@ -1,5 +1,5 @@
 """RMSNorm: the reference's test pattern (kernels tests/test_rmsnorm.py) on the
-B200 kernels, plus oracle parity and the BASELINE sweep (row 0 fixed, B in
+B200 kernels, plus oracle parity and the headline invariance sweep (row 0 fixed, B in
 {1, 64}, 100 runs, bitwise)."""
 import numpy as np
 import pytest

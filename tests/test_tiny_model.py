@@ -1,5 +1,5 @@
 """TinyModel: the reference's tests (tests/test_tiny_model.py), the serving
-engine against the reference-style eager loop, oracle parity, and the BASELINE
+engine against the reference-style eager loop, oracle parity, and the benchmark
 decode config (4 L, d 1024, 16 x 64, SwiGLU 2816, vocab 32000; a tracked
 32-token prompt among 0/7/63/255 ragged prompts; 128 greedy tokens)."""
 import numpy as np
@@ -77,7 +77,7 @@ def _oracle_weights(model):
 
 
 def test_first_step_logits_match_oracle(dev):
-    """One decode step of a BASELINE-shaped model (bf16, SwiGLU): logits within
+    """One decode step of a benchmark-shaped model (bf16, SwiGLU): logits within
     bf16 tolerance of the f32 oracle."""
     import torch
     from detkernels_b200.kernels.tiny_model import TinyModel, TinyModelConfig
